@@ -1,0 +1,726 @@
+"""Benchmark of the paged-KV hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode_bf16|decode_int8|decode_fp32|longctx|migrate]
+
+Default workload: Llama-3-8B-shaped bf16 decode attention, 32 query
+heads over 8 KV heads, head_dim 128, block 16, 64 sequences with context lengths
+U[512, 8192] per GPU, pages a random permutation of the pool.  One step = one decode
+attention launch over the batch.  At N GPUs each rank decodes its own 64-sequence
+batch (sequences are independent units; no collective on the data path): weak scaling.
+
+Other workloads (run by hand, one JSON line each): decode_int8 (config 3), decode_fp32,
+longctx (config 5, KV heads sharded over the ranks, strong scaling), migrate (config 4,
+prefill ranks push KV blocks to decode ranks over NVLink).
+
+--impl reference times the reference's own CPU algorithm for the same workload: the
+C restatement in oracle/ (the reference is Java; no JDK exists here), all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "paged-decode attn tokens/s + HBM GB/s vs 8 TB/s; KV migration GB/s vs NVLink"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode_bf16",
+                    choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate"])
+    ap.add_argument("--seed", type=int, default=2024)
+    ap.add_argument("--gather", action="store_true", help="longctx: all-gather head-sharded outputs")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_per_launch(workload):
+    """ncu dram bytes per launch of the dominant kernel, from the committed summary."""
+    p = os.path.join(ROOT, "profiles", f"ncu_{workload}.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------ workloads
+
+def decode_shape(workload):
+    if workload == "longctx":
+        return dict(hq=64, hkv=8, d=128, bs=16, batch=256, lo=4096, hi=131072, dist="loguniform")
+    return dict(hq=32, hkv=8, d=128, bs=16, batch=64, lo=512, hi=8192, dist="uniform")
+
+
+def context_lengths(shape, rng):
+    import numpy as np
+    if shape["dist"] == "uniform":
+        return rng.integers(shape["lo"], shape["hi"] + 1, shape["batch"]).astype(np.int32)
+    u = rng.uniform(math.log(shape["lo"]), math.log(shape["hi"]), shape["batch"])
+    return np.exp(u).astype(np.int32)
+
+
+class DecodeBatch:
+    """Synthetic decode batch resident in HBM: pool, tables, q, output."""
+
+    def __init__(self, workload, seed, device, head_lo=0, head_hi=None):
+        import numpy as np
+        import torch
+        sh = decode_shape(workload)
+        self.workload = workload
+        self.sh = sh
+        rng = np.random.default_rng(seed)
+        self.ctx_np = context_lengths(sh, rng)
+        B, BS, D = sh["batch"], sh["bs"], sh["d"]
+        hkv_all = sh["hkv"]
+        head_hi = hkv_all if head_hi is None else head_hi
+        self.hkv = head_hi - head_lo
+        self.hq = sh["hq"] // hkv_all * self.hkv
+        need = (self.ctx_np + BS - 1) // BS
+        self.nb = int(need.sum())
+        perm = rng.permutation(self.nb).astype(np.int32)
+        self.maxb = int(need.max())
+        bt = np.zeros((B, self.maxb), np.int32)
+        off = 0
+        for s in range(B):
+            bt[s, :need[s]] = perm[off:off + need[s]]
+            off += need[s]
+        self.bt_np = bt
+        self.device = device
+        g = torch.Generator(device=device).manual_seed(seed)
+        kv_dt = {"decode_fp32": torch.float32}.get(workload, torch.bfloat16)
+        q_dt = torch.float32 if workload == "decode_fp32" else torch.bfloat16
+        std = 1.0 if workload == "decode_fp32" else 0.5
+        shape = (self.nb, self.hkv, BS, D)
+        self.k = self._randn(shape, std, kv_dt, g)
+        self.v = self._randn(shape, std, kv_dt, g)
+        self.k_scales = self.v_scales = None
+        self.scale_strides = (0, 0, 0)
+        if workload == "decode_int8":
+            self.k, self.k_scales = self._quant_pages(self.k)
+            self.v, self.v_scales = self._quant_pages(self.v)
+            self.scale_strides = (self.hkv, 1, 0)
+        self.q = (torch.randn((B, self.hq, D), generator=g, device=device) * 1.0).to(q_dt)
+        self.bt = torch.from_numpy(bt).to(device)
+        self.ctx = torch.from_numpy(self.ctx_np).to(device)
+        self.out = torch.empty_like(self.q)
+        self.kv_elem = self.k.element_size()
+        self.q_elem = self.q.element_size()
+
+    @staticmethod
+    def _randn(shape, std, dt, g):
+        import torch
+        t = torch.empty(shape, dtype=dt, device=g.device)
+        flat = t.view(-1)
+        step = 1 << 28
+        for i in range(0, flat.numel(), step):
+            n = min(step, flat.numel() - i)
+            flat[i:i + n] = (torch.randn(n, generator=g, device=g.device) * std).to(dt)
+        return t
+
+    @staticmethod
+    def _quant_pages(x):
+        """Per-(page, kv-head) symmetric int8 of bf16 values: scale = max|x|/127."""
+        import torch
+        nb = x.shape[0]
+        q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+        sc = torch.empty(x.shape[:2], dtype=torch.float32, device=x.device)
+        step = 1 << 14
+        for i in range(0, nb, step):
+            xs = x[i:i + step].float()
+            amax = xs.abs().amax(dim=(2, 3))
+            s = torch.where(amax == 0, torch.ones_like(amax), amax / 127.0)
+            q[i:i + step] = torch.clamp(torch.floor(xs / s[:, :, None, None] + 0.5), -127, 127).to(torch.int8)
+            sc[i:i + step] = s
+        return q, sc
+
+    def algorithmic_bytes(self):
+        """Bytes one decode step must move: every context token's K and V row of each
+        kv-head, the scales, q, out, the used block-table entries and the lengths."""
+        sh = self.sh
+        tok = int(self.ctx_np.sum())
+        kv = tok * self.hkv * sh["d"] * self.kv_elem * 2
+        pages = int(((self.ctx_np + sh["bs"] - 1) // sh["bs"]).sum())
+        scales = pages * self.hkv * 4 * 2 if self.k_scales is not None else 0
+        qo = 2 * self.q.numel() * self.q_elem
+        return kv + scales + qo + pages * 4 + len(self.ctx_np) * 4
+
+    def run(self, out=None, q=None, bt=None, ctx=None, stream=None):
+        from gollek_b200 import ops
+        return ops.paged_attention(q if q is not None else self.q, self.k, self.v,
+                                   bt if bt is not None else self.bt,
+                                   ctx if ctx is not None else self.ctx,
+                                   num_kv_heads=self.hkv, block_size=self.sh["bs"],
+                                   num_blocks=self.nb, k_scales=self.k_scales,
+                                   v_scales=self.v_scales, scale_strides=self.scale_strides,
+                                   out=out if out is not None else self.out, stream=stream)
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown", 0x1: "gpu_idle",
+               0x2: "applications_clocks_setting"}
+
+    def __init__(self, index, period=0.002):
+        self.index, self.period = index, period
+        self.samples, self.reasons = [], 0
+        self._stop = threading.Event()
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _loop(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                self.reasons |= fn(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._loop, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ distributed
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+def cpu_decode_baseline(batch, seconds, threads=None):
+    """The reference's CPU algorithm (oracle restatement of PagedAttentionVectorAPI) on
+    fp32 copies of the same values, all host threads, whole batch per step."""
+    import numpy as np
+    from oracle import oracle as O
+    threads = threads or O.num_threads()
+    q = batch.q.float().cpu().numpy()
+    bt, ctx = batch.bt_np, batch.ctx_np
+    # int8 pages: the oracle's INT8 storage with per-token scales (the page scale repeated)
+    if batch.k_scales is not None:
+        k = batch.k.cpu().numpy()
+        v = batch.v.cpu().numpy()
+        bs = batch.sh["bs"]
+        ks = np.repeat(batch.k_scales.cpu().numpy()[:, :, None], bs, axis=2)
+        vs = np.repeat(batch.v_scales.cpu().numpy()[:, :, None], bs, axis=2)
+        storage = O.INT8
+    else:
+        k = batch.k.float().cpu().numpy()
+        v = batch.v.float().cpu().numpy()
+        ks = vs = None
+        storage = O.FP32
+    scale = 1.0 / math.sqrt(batch.sh["d"])
+    # bounded sample: grow the number of sequences until one call takes ~1/3 of the budget
+    B = len(ctx)
+    n = 1
+    while True:
+        t0 = time.perf_counter()
+        O.a2_compute(q[:n, None], k, v, bt[:n], ctx[:n], scale, storage=storage,
+                     num_kv_heads=batch.hkv, block_size=batch.sh["bs"], k_scale=ks, v_scale=vs,
+                     threads=threads)
+        dt = time.perf_counter() - t0
+        if n >= B or dt > seconds / 3:
+            break
+        n = min(B, n * 2)
+    reps, total, t_start = 0, 0.0, time.perf_counter()
+    while time.perf_counter() - t_start < seconds and reps < 1000:
+        t0 = time.perf_counter()
+        O.a2_compute(q[:n, None], k, v, bt[:n], ctx[:n], scale, storage=storage,
+                     num_kv_heads=batch.hkv, block_size=batch.sh["bs"], k_scale=ks, v_scale=vs,
+                     threads=threads)
+        total += time.perf_counter() - t0
+        reps += 1
+    per_seq = total / (reps * n)
+    # tokens/s over the whole batch: the sample's time per sequence, weighted by context
+    frac = float(ctx[:n].sum()) / float(ctx.sum())
+    t_step = (total / reps) / frac
+    return {"value": B / t_step, "unit": "tokens/s", "cores": int(threads), "kind": "port",
+            "sample": f"{n} of {B} sequences ({frac:.1%} of the batch's context tokens), "
+                      f"{reps} repetitions, {total:.1f} s; scaled to the full batch by context "
+                      f"tokens; oracle/oracle.c a2 (PagedAttentionVectorAPI restatement), "
+                      f"fp32 values, OpenMP over (sequence, q-head)",
+            "seconds_per_step": t_step, "per_seq_s": per_seq}
+
+
+# ------------------------------------------------------------------ decode bench
+
+def bench_decode(args, world, rank, local):
+    import numpy as np
+    import torch
+    from gollek_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if args.workload == "longctx":
+        hkv_all = decode_shape("longctx")["hkv"]
+        per = hkv_all // world
+        batch = DecodeBatch("longctx", args.seed, dev, head_lo=rank * per, head_hi=(rank + 1) * per)
+    else:
+        batch = DecodeBatch(args.workload, args.seed + rank, dev)
+    stream = torch.cuda.current_stream(dev)
+    gather_buf = None
+    if args.workload == "longctx" and args.gather and world > 1:
+        import torch.distributed as dist
+        gather_buf = torch.empty((world,) + tuple(batch.out.shape), dtype=batch.out.dtype, device=dev)
+
+    def step():
+        batch.run()
+        if gather_buf is not None:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(gather_buf, batch.out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_ms = e0.elapsed_time(e1)
+    t_ms_max = max_over_ranks(t_ms, world)
+    B = len(batch.ctx_np)
+    launches = args.steps * (1 + (1 if gather_buf is not None else 0))
+
+    # ---------------- e2e: host buffers in, host result out, through the C ABI
+    from gollek_b200 import _lib
+    B, Hq, D = batch.q.shape
+    hq_pin = batch.q.cpu().pin_memory()
+    hbt_pin = batch.bt.cpu().pin_memory()
+    hctx_pin = batch.ctx.cpu().pin_memory()
+    hout_pin = torch.empty(batch.out.shape, dtype=batch.out.dtype).pin_memory()
+    append = args.workload in ("decode_bf16", "decode_fp32", "longctx")
+    if append:
+        g = torch.Generator().manual_seed(args.seed + 7)
+        kv_dt = batch.k.dtype
+        hk_new = torch.randn((B, batch.hkv, D), generator=g).to(kv_dt).pin_memory()
+        hv_new = torch.randn((B, batch.hkv, D), generator=g).to(kv_dt).pin_memory()
+        hpos = (batch.ctx.cpu() - 1).to(torch.int32).pin_memory()
+    dq, dbt, dctx = torch.empty_like(batch.q), torch.empty_like(batch.bt), torch.empty_like(batch.ctx)
+    if append:
+        dk_new = torch.empty((B, batch.hkv, D), dtype=batch.k.dtype, device=dev)
+        dv_new = torch.empty_like(dk_new)
+        dpos = torch.empty((B,), dtype=torch.int32, device=dev)
+
+    def e2e_step():
+        dq.copy_(hq_pin, non_blocking=True)
+        dbt.copy_(hbt_pin, non_blocking=True)
+        dctx.copy_(hctx_pin, non_blocking=True)
+        if append:
+            dk_new.copy_(hk_new, non_blocking=True)
+            dv_new.copy_(hv_new, non_blocking=True)
+            dpos.copy_(hpos, non_blocking=True)
+            ops.kv_append(dk_new, dv_new, dpos, dbt, batch.k, batch.v, block_size=batch.sh["bs"],
+                          num_blocks=batch.nb)
+        batch.run(q=dq, bt=dbt, ctx=dctx)
+        hout_pin.copy_(batch.out, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 100))
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    h2d = (hq_pin.numel() * hq_pin.element_size() + hbt_pin.numel() * 4 + hctx_pin.numel() * 4)
+    if append:
+        h2d += 2 * hk_new.numel() * hk_new.element_size() + hpos.numel() * 4
+    d2h = hout_pin.numel() * hout_pin.element_size()
+
+    if args.workload == "longctx":
+        total_seqs = B  # every rank processes all sequences for its heads
+    else:
+        total_seqs = B * world
+    value = total_seqs * args.steps / (t_ms_max / 1e3)
+    e2e_value = total_seqs * e2e_steps / (e2e_ms / 1e3)
+
+    # roofline of the decode kernel (this rank's launch; max over ranks)
+    alg = batch.algorithmic_bytes()
+    per_launch_s = (t_ms / 1e3) / args.steps
+    achieved = alg / per_launch_s / 1e9
+    achieved_min = -max_over_ranks(-achieved, world)
+    peak, peak_kind = peaks()
+    traffic = traffic_per_launch(args.workload)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "longctx":
+        cpu = cpu_decode_baseline(batch, args.cpu_seconds)
+        cpu.pop("per_seq_s", None)
+        cpu.pop("seconds_per_step", None)
+
+    clocks = clk.summary()
+    if rank == 0:
+        sh = batch.sh
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": t_ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong" if args.workload == "longctx" else "weak",
+            "vs_baseline": None,
+            "dtype": {"decode_fp32": "f32", "decode_int8": "int8 KV, bf16 q/out, f32 accumulate"}
+            .get(args.workload, "bf16 KV/q/out, f32 accumulate"),
+            "data": "synthetic (seeded; BASELINE shapes and distributions)",
+            "config": {
+                "workload": {"decode_bf16": "config2_llama3_8b_bf16_gqa_decode",
+                             "decode_int8": "config3_int8_kv_decode",
+                             "decode_fp32": "fp32_gqa_decode",
+                             "longctx": "config5_llama3_70b_longctx_kvhead_sharded"}[args.workload],
+                "batch_per_gpu": B if args.workload != "longctx" else B,
+                "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"], "head_dim": sh["d"],
+                "block_size": sh["bs"], "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
+                "context_tokens_per_gpu": int(batch.ctx_np.sum()),
+                "kv_heads_per_gpu": batch.hkv,
+                "parallelism": (f"kv-head shard x{world}" if args.workload == "longctx"
+                                else f"independent batches x{world}"),
+                "l2": f"no flush: {alg / 1e9:.2f} GB of KV per step per GPU > 126 MB L2",
+            },
+            "hbm_gbs": achieved_min,
+            "context_tokens_per_s": float(batch.ctx_np.sum()) * (world if args.workload != "longctx" else 1)
+            * args.steps / (t_ms_max / 1e3),
+            "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
+                         "frac": achieved_min / peak, "traffic": traffic,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                         "algorithmic_bytes_per_launch": alg,
+                         "kernel": "decode_tma_kernel"},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "wall_s": wall,
+                    "path": "pinned host q/tables/lengths (+new K/V rows) -> H2D -> "
+                            "gollek_kv_append -> gollek_paged_attention_v2 -> D2H out"
+                            if append else
+                            "pinned host q/tables/lengths -> H2D -> gollek_paged_attention_v2 -> D2H out",
+                    "gpu_launches_per_step": 2 if append else 1},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ migration bench
+
+def migrate_plan(seed, world):
+    """Requests, their prefill (source) rank and block counts; config 4 shapes."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    lens = np.exp(rng.uniform(math.log(2048), math.log(32768), 64)).astype(np.int64)
+    nsrc = max(1, world // 2)
+    src_rank = np.arange(64) % nsrc
+    blocks = (lens + 15) // 16
+    return lens, src_rank, blocks, nsrc
+
+
+def bench_migrate(args, world, rank, local):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from gollek_b200 import _lib, ops
+    if world < 2:
+        raise SystemExit("migrate needs --gpus >= 2 (prefill ranks push to decode ranks)")
+    dev = torch.device("cuda", local)
+    L, H, BS, D = 32, 8, 16, 128
+    bpb = BS * H * D * 2  # bytes per (block, layer), bf16: 32 KiB
+    blk = L * bpb         # one block, all layers: 1 MiB, per K and per V
+    lens, src_rank, blocks, nsrc = migrate_plan(args.seed, world)
+    is_src = rank < nsrc
+    peer = rank + nsrc if is_src else rank - nsrc
+    mine = np.where(src_rank == (rank if is_src else peer))[0]
+    nblk = int(blocks[mine].sum())
+    rng = np.random.default_rng(args.seed + 100 + (rank if is_src else peer))
+    # prefill pool: requests' blocks at permuted positions; decode pool: random free list
+    pool_blocks = nblk + 64
+    src_ids = rng.permutation(pool_blocks)[:nblk].astype(np.int32)
+    dst_ids = rng.permutation(pool_blocks)[:nblk].astype(np.int32)
+    k = torch.empty(pool_blocks * blk, dtype=torch.uint8, device=dev)
+    v = torch.empty_like(k)
+    if is_src:
+        g = torch.Generator(device=dev).manual_seed(args.seed + rank)
+        for t in (k, v):
+            fl = t.view(torch.bfloat16)
+            step = 1 << 28
+            for i in range(0, fl.numel(), step):
+                n = min(step, fl.numel() - i)
+                fl[i:i + n] = torch.randn(n, generator=g, device=dev).to(torch.bfloat16)
+    else:
+        k.zero_()
+        v.zero_()
+    # exchange the decode pools' IPC handles
+    import ctypes
+    lib = _lib.load()
+    hk = (ctypes.c_char * 64)()
+    hv = (ctypes.c_char * 64)()
+    if not is_src:
+        _lib.check(lib.gollek_ipc_get_handle(ctypes.c_void_p(k.data_ptr()), hk))
+        _lib.check(lib.gollek_ipc_get_handle(ctypes.c_void_p(v.data_ptr()), hv))
+    handles = [None] * world
+    dist.all_gather_object(handles, (bytes(hk), bytes(hv)) if not is_src else None)
+    torch.cuda.synchronize()
+    dk_ptr = dv_ptr = None
+    if is_src:
+        hk_b, hv_b = handles[peer]
+        pk, pv = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(lib.gollek_ipc_open_handle(hk_b, ctypes.byref(pk)))
+        _lib.check(lib.gollek_ipc_open_handle(hv_b, ctypes.byref(pv)))
+        dk_ptr, dv_ptr = pk.value, pv.value
+    s_ids = torch.from_numpy(src_ids).to(dev)
+    d_ids = torch.from_numpy(dst_ids).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        if is_src:
+            ops.kv_migrate(k, v, None, None, s_ids, d_ids, src_block_stride=blk, dst_block_stride=blk,
+                           bytes_per_block=blk, device=local, dst_k_ptr=dk_ptr, dst_v_ptr=dv_ptr)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_ms = e0.elapsed_time(e1) if is_src else 0.0
+    t_max = max_over_ranks(t_ms, world)
+    # verification: per-block checksums on both sides must agree (bit-exact copy)
+    ids = s_ids if is_src else d_ids
+    ck = ops.block_checksums(k, ids, block_stride=blk, bytes_per_block=blk).cpu().numpy()
+    cv = ops.block_checksums(v, ids, block_stride=blk, bytes_per_block=blk).cpu().numpy()
+    gathered = [None] * world
+    dist.all_gather_object(gathered, (ck, cv))
+    ok = all(np.array_equal(gathered[r][0], gathered[r + nsrc][0]) and
+             np.array_equal(gathered[r][1], gathered[r + nsrc][1]) for r in range(nsrc))
+    bytes_total = int(blocks.sum()) * blk * 2
+    if is_src:
+        lib.gollek_ipc_close_handle(ctypes.c_void_p(dk_ptr))
+        lib.gollek_ipc_close_handle(ctypes.c_void_p(dv_ptr))
+    barrier(world)
+    if rank == 0:
+        gbs = bytes_total * args.steps / (t_max / 1e3) / 1e9
+        peak = 770.0 * nsrc
+        print(json.dumps({
+            "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "u8 (bf16 KV bytes)",
+            "data": "synthetic (seeded; BASELINE config 4 shapes)",
+            "config": {"workload": "config4_prefill_to_decode_migration", "layers": L,
+                       "kv_heads": H, "head_dim": D, "block_size": BS, "requests": 64,
+                       "prompt": "loguniform[2048,32768]", "blocks": int(blocks.sum()),
+                       "bytes_per_step": bytes_total, "sources": nsrc, "destinations": nsrc,
+                       "parallelism": f"{nsrc} prefill ranks -> {nsrc} decode ranks, NVLink P2P push"},
+            "bit_exact": bool(ok),
+            "roofline": {"bound": "nvlink", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "traffic": None,
+                         "peak_source": "770 GB/s measured peer copy per direction per source GPU"},
+            "gpu_launches": args.steps * nsrc, "clocks": clk.summary(), "cpu_baseline": None,
+        }), flush=True)
+
+
+# ------------------------------------------------------------------ reference arm
+
+def bench_reference(args):
+    """The reference's CPU decode algorithm on the host cores (rank 0 only)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle as O
+    if args.workload == "migrate":
+        print(json.dumps({"impl": "reference", "unavailable": "migrate: the reference copies "
+                          "within one host pool; run --workload migrate for the GPU arm only"}))
+        return
+
+    class HostBatch:
+        pass
+
+    import torch
+    sh = decode_shape(args.workload)
+    rng = np.random.default_rng(args.seed)
+    ctx = context_lengths(sh, rng)
+    B, BS, D = sh["batch"], sh["bs"], sh["d"]
+    need = (ctx + BS - 1) // BS
+    nb = int(need.sum())
+    perm = rng.permutation(nb).astype(np.int32)
+    bt = np.zeros((B, int(need.max())), np.int32)
+    off = 0
+    for s in range(B):
+        bt[s, :need[s]] = perm[off:off + need[s]]
+        off += need[s]
+    hkv = sh["hkv"]
+    if args.workload == "longctx":
+        hkv = max(1, hkv // max(world, 1))
+    hq = sh["hq"] // sh["hkv"] * hkv
+    g = torch.Generator().manual_seed(args.seed)
+    std = 1.0 if args.workload == "decode_fp32" else 0.5
+    hb = HostBatch()
+    hb.sh, hb.hkv, hb.ctx_np, hb.bt_np = sh, hkv, ctx, bt
+    # values rounded to bf16 as on the GPU arm (fp32 stays fp32)
+    to = torch.float32 if args.workload == "decode_fp32" else torch.bfloat16
+    hb.q = torch.randn((B, hq, D), generator=g).to(to)
+    hb.k = (torch.randn((nb, hkv, BS, D), generator=g) * std).to(to)
+    hb.v = (torch.randn((nb, hkv, BS, D), generator=g) * std).to(to)
+    hb.k_scales = hb.v_scales = None
+    if args.workload == "decode_int8":
+        def qp(x):
+            xs = x.float()
+            amax = xs.abs().amax(dim=(2, 3))
+            s = torch.where(amax == 0, torch.ones_like(amax), amax / 127.0)
+            return torch.clamp(torch.floor(xs / s[:, :, None, None] + 0.5), -127, 127).to(torch.int8), s
+        hb.k, hb.k_scales = qp(hb.k)
+        hb.v, hb.v_scales = qp(hb.v)
+    per_step_budget = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
+    r = cpu_decode_baseline(hb, per_step_budget * (args.steps + args.warmup))
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": r["seconds_per_step"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (reference CPU path)", "data": "synthetic (seeded; same shapes as ours)",
+        "config": {"workload": args.workload, "batch": B, "num_q_heads": hq, "num_kv_heads": hkv,
+                   "head_dim": D, "block_size": BS},
+        "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"],
+                         "kind": r["kind"], "sample": r["sample"]},
+        "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        bench_reference(args)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        if args.workload == "migrate":
+            bench_migrate(args, world, rank, local)
+        else:
+            bench_decode(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

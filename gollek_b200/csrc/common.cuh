@@ -1,0 +1,151 @@
+// common.cuh -- shared device helpers for the sm_100a paged-KV kernels:
+// element decoding, mbarrier / TMA / cp.async wrappers, bounded waits and the
+// per-device status word.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gollek_kernels.h"
+
+namespace gk {
+
+// Sticky per-device status word (GOLLEK_STATUS_* bits).  Kernels OR bits into it;
+// the host reads and clears it with gollek_device_status().
+__device__ unsigned int g_status;
+
+__device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
+
+// Iterations of a try_wait loop before a wait gives up and reports
+// GOLLEK_STATUS_TIMEOUT.  Each try_wait blocks for a hardware-defined slice, so
+// this bounds a wait at well over a second: far beyond any real TMA latency.
+constexpr unsigned kWaitLimit = 1u << 24;
+
+// ----------------------------------------------------------------- elements
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// ----------------------------------------------------------------- mbarrier
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase of `bar` with the given parity.  Returns false (and
+// raises GOLLEK_STATUS_TIMEOUT) if it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    for (unsigned i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    raise_status(GOLLEK_STATUS_TIMEOUT);
+    return false;
+}
+
+// --------------------------------------------------------------- TMA / async
+
+// 2-D tiled TMA load (no multicast) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 4-byte cp.async (Ampere-style) global -> shared.
+__device__ __forceinline__ void cp_async_4(void *smem_dst, const void *gsrc) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+
+// Arrive on `bar` once this thread's earlier cp.async copies have landed; the
+// arrival counts against the barrier's expected count.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// --------------------------------------------------------------------- math
+
+// 2^x with the hardware's approximate exponent (ex2.approx, flush-to-zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Named barrier over `count` threads (a multiple of 32), id 1..15.
+__device__ __forceinline__ void named_barrier(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Math.round(float): closest integer, ties toward +infinity; NaN -> 0.
+// (double)x + 0.5 is exact for every float below 2^29, so floor gives the
+// correctly rounded result.
+__device__ __forceinline__ int java_round(float x) {
+    if (x != x) return 0;
+    double r = floor(static_cast<double>(x) + 0.5);
+    r = fmin(fmax(r, -2147483648.0), 2147483647.0);
+    return static_cast<int>(r);
+}
+
+}  // namespace gk

@@ -1,0 +1,689 @@
+// gollek_kernels.cu -- host side of libgollek_kernels.so: argument checks, kernel
+// selection, TMA descriptors, per-(device, stream) scratch and the C ABI declared
+// in include/gollek_kernels.h.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "common.cuh"
+#include "decode_generic.cuh"
+#include "decode_tma.cuh"
+#include "kv_append.cuh"
+#include "kv_migrate.cuh"
+
+namespace gk {
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    cudaGetLastError();  // clear a non-sticky error so the next call starts clean
+    return fail(static_cast<int>(e), "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define GK_CUDA(call, what)                        \
+    do {                                           \
+        cudaError_t e_ = (call);                   \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (dev >= 0 && dev != prev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// ----------------------------------------------------------- driver entry points
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    std::call_once(g_encode_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        cudaGetLastError();
+    });
+    return g_encode;
+}
+
+// ------------------------------------------------------------------ device info
+
+std::mutex g_mu;
+std::map<int, int> g_sm_count;
+std::map<std::pair<int, void *>, std::pair<void *, size_t>> g_ws;  // (device, stream) -> scratch
+
+int sm_count(int dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_sm_count.find(dev);
+    if (it != g_sm_count.end()) return it->second;
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = n;
+    return n;
+}
+
+// Library-owned split-K scratch for (device, stream), zero-filled when (re)allocated.
+int library_workspace(int dev, void *stream, size_t bytes, void **out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto &slot = g_ws[{dev, stream}];
+    if (slot.second < bytes) {
+        if (slot.first) {
+            cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+            cudaFree(slot.first);
+            slot = {nullptr, 0};
+        }
+        void *p = nullptr;
+        GK_CUDA(cudaMalloc(&p, bytes), "cudaMalloc(split-K workspace)");
+        GK_CUDA(cudaMemsetAsync(p, 0, bytes, static_cast<cudaStream_t>(stream)),
+                "cudaMemsetAsync(split-K workspace)");
+        slot = {p, bytes};
+    }
+    *out = slot.first;
+    return GOLLEK_OK;
+}
+
+int dtype_bytes(int dt) {
+    switch (dt) {
+        case GOLLEK_DTYPE_F32:
+            return 4;
+        case GOLLEK_DTYPE_BF16:
+        case GOLLEK_DTYPE_F16:
+            return 2;
+        case GOLLEK_DTYPE_I8:
+            return 1;
+        default:
+            return 0;
+    }
+}
+
+size_t ws_counters_bytes(int S, int Hkv) {
+    return align_up(static_cast<uint32_t>(S) * Hkv * 4u, 256u);
+}
+
+size_t ws_bytes(int S, int Hq, int Hkv, int D) {
+    const int G = Hq / Hkv;
+    const size_t slot = static_cast<size_t>(2 * G + G * D) * 4;
+    return ws_counters_bytes(S, Hkv) + static_cast<size_t>(S) * Hkv * kMaxSplits * slot;
+}
+
+// ------------------------------------------------------------------ fast path
+
+constexpr int kNC = 4;                  // consumer warps per CTA
+constexpr uint32_t kSmemBudget = 112 * 1024;  // per CTA: two CTAs share an SM's 228 KB
+constexpr int kMinChunkGroups = 4;      // split-K chunk >= 128 tokens
+constexpr int kItemsPerCta = 4;
+
+struct Launch {
+    const void *fn;
+    int kv_bytes;
+    bool quant;
+};
+
+template <typename KV, int D, int G>
+const void *fast_kernel() {
+    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, kNC>);
+}
+
+template <typename KV, int D>
+const void *pick_g(int G) {
+    switch (G) {
+        case 1: return fast_kernel<KV, D, 1>();
+        case 2: return fast_kernel<KV, D, 2>();
+        case 4: return fast_kernel<KV, D, 4>();
+        case 8: return fast_kernel<KV, D, 8>();
+        default: return nullptr;
+    }
+}
+
+const void *pick_fast(int kv, int D, int G) {
+    switch (kv) {
+        case GOLLEK_DTYPE_BF16:
+            return D == 128 ? pick_g<__nv_bfloat16, 128>(G) : D == 64 ? pick_g<__nv_bfloat16, 64>(G) : nullptr;
+        case GOLLEK_DTYPE_F16:
+            return D == 128 ? pick_g<__half, 128>(G) : D == 64 ? pick_g<__half, 64>(G) : nullptr;
+        case GOLLEK_DTYPE_F32:
+            return D == 128 ? pick_g<float, 128>(G) : D == 64 ? pick_g<float, 64>(G) : nullptr;
+        case GOLLEK_DTYPE_I8:
+            return D == 128 ? pick_g<int8_t, 128>(G) : nullptr;
+        default:
+            return nullptr;
+    }
+}
+
+CUtensorMapDataType tma_type(int kv) {
+    switch (kv) {
+        case GOLLEK_DTYPE_F32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        case GOLLEK_DTYPE_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        case GOLLEK_DTYPE_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+        default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct V2 {
+    void *out;
+    const void *q, *k, *v;
+    const float *ks, *vs;
+    const int *bt, *ctx;
+    int S, Hq, Hkv, D, BS, maxB, num_blocks;
+    long long page_stride;
+    int q_dtype, kv_dtype;
+    long long sps, shs, sts;
+    float scale, soft_cap;
+    int window;
+    float norm_eps;
+    void *workspace;
+    size_t workspace_bytes;
+    void *stream;
+};
+
+int encode_map(CUtensorMap *m, const void *base, int kv, int D, long long rows, int box_rows) {
+    auto enc = encode_fn();
+    if (!enc) return fail(GOLLEK_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    const int eb = dtype_bytes(kv);
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * eb};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / eb), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, tma_type(kv), 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GOLLEK_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return GOLLEK_OK;
+}
+
+// Eligibility of the TMA kernel; returns its function or nullptr.
+const void *fast_eligible(const V2 &p, int G, long long page_stride) {
+    const int eb = dtype_bytes(p.kv_dtype);
+    if (eb == 0) return nullptr;
+    const void *fn = pick_fast(p.kv_dtype, p.D, G);
+    if (!fn) return nullptr;
+    const bool bs_ok = (p.BS >= 8 && p.BS <= 32 && 32 % p.BS == 0) || (p.BS > 32 && p.BS % 32 == 0);
+    if (!bs_ok) return nullptr;
+    if (!aligned16(p.k) || !aligned16(p.v)) return nullptr;
+    if (page_stride % p.D != 0 || (page_stride * eb) % 16 != 0) return nullptr;
+    if (p.S > kMaxFastSeqs) return nullptr;
+    if (p.kv_dtype == GOLLEK_DTYPE_I8 && (!p.ks || !p.vs)) return nullptr;
+    if (p.q_dtype != GOLLEK_DTYPE_F32 && p.q_dtype != GOLLEK_DTYPE_BF16) return nullptr;
+    const long long rows_per_page = page_stride / p.D;
+    if (p.num_blocks > 0 && static_cast<long long>(p.num_blocks) * rows_per_page >= (1LL << 31))
+        return nullptr;
+    return fn;
+}
+
+int run_v2(const V2 &p) {
+    int dev = 0;
+    GK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    const int G = p.Hq / p.Hkv;
+    const long long page_stride =
+        p.page_stride > 0 ? p.page_stride : static_cast<long long>(p.Hkv) * p.BS * p.D;
+    const float log2e = kLog2e;
+    const bool cap = p.soft_cap > 0.f;
+    cudaStream_t st = static_cast<cudaStream_t>(p.stream);
+    if (p.S == 0) return GOLLEK_OK;
+
+    const void *fn = fast_eligible(p, G, page_stride);
+    if (fn) {
+        const int eb = dtype_bytes(p.kv_dtype);
+        const bool quant = p.kv_dtype == GOLLEK_DTYPE_I8;
+        const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * kSlabBytes;
+        DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, kNC, 0, p.S);
+        int stages = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / (2 * tile));
+        stages = std::min(std::max(stages, 2), 16);
+        DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, kNC, stages, p.S);
+        if (L.total > 227 * 1024) fn = nullptr;
+        if (fn) {
+            void *ws = p.workspace;
+            const size_t need = ws_bytes(p.S, p.Hq, p.Hkv, p.D);
+            if (ws) {
+                if (p.workspace_bytes < need)
+                    return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed",
+                                p.workspace_bytes, need);
+            } else {
+                int rc = library_workspace(dev, p.stream, need, &ws);
+                if (rc) return rc;
+            }
+            const long long rows_per_page = page_stride / p.D;
+            const long long rows = p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page
+                                                    : (1LL << 31) - 1;
+            const int box_rows = p.BS < kRows ? p.BS : kRows;
+            CUtensorMap tmk, tmv;
+            int rc = encode_map(&tmk, p.k, p.kv_dtype, p.D, rows, box_rows);
+            if (!rc) rc = encode_map(&tmv, p.v, p.kv_dtype, p.D, rows, box_rows);
+            if (rc) return rc;
+
+            DecodeArgs a;
+            a.out = p.out;
+            a.q = p.q;
+            a.k_scales = p.ks;
+            a.v_scales = p.vs;
+            a.block_tables = p.bt;
+            a.context_lens = p.ctx;
+            a.counters = static_cast<int *>(ws);
+            a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ws_counters_bytes(p.S, p.Hkv));
+            a.page_rows = rows_per_page;
+            a.scale_page_stride = p.sps;
+            a.scale_head_stride = p.shs;
+            a.scale_token_stride = p.sts;
+            a.num_seqs = p.S;
+            a.num_kv_heads = p.Hkv;
+            a.block_size = p.BS;
+            a.max_blocks = p.maxB;
+            a.num_blocks = p.num_blocks;
+            a.window = p.window;
+            a.q_bf16 = p.q_dtype == GOLLEK_DTYPE_BF16;
+            a.num_stages = stages;
+            a.min_chunk_groups = kMinChunkGroups;
+            a.items_per_cta = kItemsPerCta;
+            a.q_scale = cap ? p.scale : p.scale * log2e;
+            a.soft_cap = p.soft_cap;
+            a.post_scale = cap ? log2e : 1.f;
+            a.norm_eps = p.norm_eps;
+
+            GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
+                    "cudaFuncSetAttribute");
+            int per_sm = 0;
+            GK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, (kNC + 1) * 32, L.total),
+                    "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+            if (per_sm < 1) per_sm = 1;
+            const int grid = sm_count(dev) * per_sm;
+            void *args[] = {&tmk, &tmv, &a};
+            GK_CUDA(cudaLaunchKernel(fn, dim3(grid), dim3((kNC + 1) * 32), args, L.total, st),
+                    "decode_tma_kernel launch");
+            return GOLLEK_OK;
+        }
+    }
+
+    // Generic kernel.
+    if (G > kGenMaxG || p.D > kGenMaxJ * 32)
+        return fail(GOLLEK_ERR_UNSUPPORTED, "head_dim %d / GQA group %d outside the supported range",
+                    p.D, G);
+    GenericArgs g;
+    g.out = p.out;
+    g.q = p.q;
+    g.k = p.k;
+    g.v = p.v;
+    g.k_scales = p.ks;
+    g.v_scales = p.vs;
+    g.block_tables = p.bt;
+    g.context_lens = p.ctx;
+    g.page_stride = page_stride;
+    g.scale_page_stride = p.sps;
+    g.scale_head_stride = p.shs;
+    g.scale_token_stride = p.sts;
+    g.num_q_heads = p.Hq;
+    g.num_kv_heads = p.Hkv;
+    g.head_dim = p.D;
+    g.block_size = p.BS;
+    g.max_blocks = p.maxB;
+    g.num_blocks = p.num_blocks;
+    g.window = p.window;
+    g.q_bf16 = p.q_dtype == GOLLEK_DTYPE_BF16;
+    g.kv_dtype = p.kv_dtype;
+    g.q_scale = cap ? p.scale : p.scale * log2e;
+    g.soft_cap = p.soft_cap;
+    g.post_scale = cap ? log2e : 1.f;
+    g.norm_eps = p.norm_eps;
+    decode_generic_kernel<<<dim3(p.S, p.Hkv), kGenWarps * 32, 0, st>>>(g);
+    GK_CUDA(cudaGetLastError(), "decode_generic_kernel launch");
+    return GOLLEK_OK;
+}
+
+int check_v2(const V2 &p) {
+    if (!p.out || !p.q || !p.k || !p.v || !p.bt || !p.ctx)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (p.S < 0 || p.Hq <= 0 || p.Hkv <= 0 || p.D <= 0 || p.BS <= 0 || p.maxB <= 0 || p.num_blocks < 0)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "non-positive size");
+    if (p.Hq % p.Hkv != 0)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "num_q_heads %d not a multiple of num_kv_heads %d",
+                    p.Hq, p.Hkv);
+    if (p.q_dtype != GOLLEK_DTYPE_F32 && p.q_dtype != GOLLEK_DTYPE_BF16)
+        return fail(GOLLEK_ERR_UNSUPPORTED, "q dtype %d (F32 or BF16 only)", p.q_dtype);
+    if (p.kv_dtype < GOLLEK_DTYPE_F32 || p.kv_dtype > GOLLEK_DTYPE_I4)
+        return fail(GOLLEK_ERR_UNSUPPORTED, "kv dtype %d", p.kv_dtype);
+    if ((p.kv_dtype == GOLLEK_DTYPE_I8 || p.kv_dtype == GOLLEK_DTYPE_I4) && (!p.ks || !p.vs))
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "quantised KV needs k_scales and v_scales");
+    const long long minimal = static_cast<long long>(p.Hkv) * p.BS * p.D;
+    if (p.page_stride != 0 && p.page_stride < minimal)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "page_stride %lld < num_kv_heads*block_size*head_dim",
+                    p.page_stride);
+    if (static_cast<long long>(p.maxB) * p.BS > (1LL << 30))
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "max_blocks_per_seq * block_size too large");
+    return GOLLEK_OK;
+}
+
+int read_and_clear_status(cudaStream_t st, unsigned *out) {
+    unsigned v = 0;
+    GK_CUDA(cudaMemcpyFromSymbolAsync(&v, g_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st),
+            "read status");
+    GK_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    if (v) {
+        const unsigned zero = 0;
+        GK_CUDA(cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st),
+                "clear status");
+        GK_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    }
+    *out = v;
+    return GOLLEK_OK;
+}
+
+int status_to_code(unsigned v) {
+    if (v & GOLLEK_STATUS_TIMEOUT) return fail(GOLLEK_ERR_TIMEOUT, "a device-side wait gave up");
+    if (v & GOLLEK_STATUS_BAD_BLOCK_ID)
+        return fail(GOLLEK_ERR_BAD_BLOCK_ID, "block table entry outside the pool");
+    if (v & GOLLEK_STATUS_BAD_POSITION)
+        return fail(GOLLEK_ERR_BAD_POSITION, "context length or position beyond the block table");
+    return GOLLEK_OK;
+}
+
+}  // namespace
+}  // namespace gk
+
+using namespace gk;
+
+// =============================================================== C ABI
+
+extern "C" {
+
+int paged_attention_launch(float *out, float *q, float *k_cache, float *v_cache, int *block_tables,
+                           int *context_lens, int num_seqs, int num_heads, int head_dim,
+                           int block_size, int max_blocks_per_seq, float scale) {
+    t_last_error.clear();
+    if (gollek_cuda_device_count() == 0) return fail(GOLLEK_ERR_NO_DEVICE, "no CUDA device");
+    V2 p{};
+    p.out = out;
+    p.q = q;
+    p.k = k_cache;
+    p.v = v_cache;
+    p.bt = block_tables;
+    p.ctx = context_lens;
+    p.S = num_seqs;
+    p.Hq = num_heads;
+    p.Hkv = num_heads;
+    p.D = head_dim;
+    p.BS = block_size;
+    p.maxB = max_blocks_per_seq;
+    p.num_blocks = 0;
+    p.page_stride = 0;
+    p.q_dtype = GOLLEK_DTYPE_F32;
+    p.kv_dtype = GOLLEK_DTYPE_F32;
+    p.scale = scale;
+    p.soft_cap = 0.f;
+    p.window = 0;
+    p.norm_eps = 0.f;  // the fallback divides by the plain sum (PagedAttentionCpuFallback.java:92-94)
+    p.stream = cudaStreamPerThread;
+    int rc = check_v2(p);
+    if (rc) return rc;
+    rc = run_v2(p);
+    if (rc) return rc;
+    unsigned v = 0;
+    rc = read_and_clear_status(cudaStreamPerThread, &v);
+    if (rc) return rc;
+    return status_to_code(v);
+}
+
+int gollek_cuda_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int gollek_cuda_device_name(char *buf, int len) {
+    if (!buf || len <= 0) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null or empty buffer");
+    buf[0] = 0;
+    if (gollek_cuda_device_count() == 0) return fail(GOLLEK_ERR_NO_DEVICE, "no CUDA device");
+    int dev = 0;
+    GK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    cudaDeviceProp prop;
+    GK_CUDA(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties");
+    snprintf(buf, static_cast<size_t>(len), "%s", prop.name);
+    return GOLLEK_OK;
+}
+
+int gollek_paged_attention_v2(void *out, const void *q, const void *k_cache, const void *v_cache,
+                              const float *k_scales, const float *v_scales, const int *block_tables,
+                              const int *context_lens, int num_seqs, int num_q_heads,
+                              int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq,
+                              int num_blocks, long long page_stride, int q_dtype, int kv_dtype,
+                              long long scale_page_stride, long long scale_head_stride,
+                              long long scale_token_stride, float scale, float soft_cap,
+                              int sliding_window, void *workspace, size_t workspace_bytes,
+                              void *stream) {
+    t_last_error.clear();
+    V2 p{};
+    p.out = out;
+    p.q = q;
+    p.k = k_cache;
+    p.v = v_cache;
+    p.ks = k_scales;
+    p.vs = v_scales;
+    p.bt = block_tables;
+    p.ctx = context_lens;
+    p.S = num_seqs;
+    p.Hq = num_q_heads;
+    p.Hkv = num_kv_heads;
+    p.D = head_dim;
+    p.BS = block_size;
+    p.maxB = max_blocks_per_seq;
+    p.num_blocks = num_blocks;
+    p.page_stride = page_stride;
+    p.q_dtype = q_dtype;
+    p.kv_dtype = kv_dtype;
+    p.sps = scale_page_stride;
+    p.shs = scale_head_stride;
+    p.sts = scale_token_stride;
+    p.scale = scale;
+    p.soft_cap = soft_cap;
+    p.window = sliding_window;
+    p.norm_eps = 1e-9f;  // AttentionOnlineSoftmax.NORMALIZER_EPSILON
+    p.workspace = workspace;
+    p.workspace_bytes = workspace_bytes;
+    p.stream = stream;
+    int rc = check_v2(p);
+    if (rc) return rc;
+    return run_v2(p);
+}
+
+size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
+                                             int head_dim) {
+    if (num_seqs <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0)
+        return 0;
+    return ws_bytes(num_seqs, num_q_heads, num_kv_heads, head_dim);
+}
+
+int gollek_kv_append(const void *key, const void *value, int src_dtype, const int *token_seq,
+                     const int *token_pos, const int *block_tables, int max_blocks_per_seq,
+                     int num_blocks, void *k_cache, void *v_cache, float *k_scales, float *v_scales,
+                     int kv_dtype, int num_tokens, int num_kv_heads, int head_dim, int block_size,
+                     long long page_stride, long long scale_page_stride, long long scale_head_stride,
+                     long long scale_token_stride, void *stream) {
+    t_last_error.clear();
+    if (!key || !value || !token_pos || !block_tables || !k_cache || !v_cache)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+        max_blocks_per_seq <= 0 || num_blocks < 0)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "non-positive size");
+    if (src_dtype != GOLLEK_DTYPE_F32 && src_dtype != GOLLEK_DTYPE_BF16)
+        return fail(GOLLEK_ERR_UNSUPPORTED, "source dtype %d (F32 or BF16 only)", src_dtype);
+    if (kv_dtype < GOLLEK_DTYPE_F32 || kv_dtype > GOLLEK_DTYPE_I4)
+        return fail(GOLLEK_ERR_UNSUPPORTED, "kv dtype %d", kv_dtype);
+    const long long ps = page_stride > 0 ? page_stride
+                                         : static_cast<long long>(num_kv_heads) * block_size * head_dim;
+    if (kv_dtype == GOLLEK_DTYPE_I4 && ((head_dim & 1) || (ps & 1)))
+        return fail(GOLLEK_ERR_UNSUPPORTED, "int4 pools need an even head_dim and page stride");
+    if (num_tokens == 0) return GOLLEK_OK;
+    AppendArgs a;
+    a.key = key;
+    a.value = value;
+    a.token_seq = token_seq;
+    a.token_pos = token_pos;
+    a.block_tables = block_tables;
+    a.k = k_cache;
+    a.v = v_cache;
+    a.k_scales = k_scales;
+    a.v_scales = v_scales;
+    a.page_stride = ps;
+    a.scale_page_stride = scale_page_stride;
+    a.scale_head_stride = scale_head_stride;
+    a.scale_token_stride = scale_token_stride;
+    a.src_bf16 = src_dtype == GOLLEK_DTYPE_BF16;
+    a.kv_dtype = kv_dtype;
+    a.num_tokens = num_tokens;
+    a.num_kv_heads = num_kv_heads;
+    a.head_dim = head_dim;
+    a.block_size = block_size;
+    a.max_blocks = max_blocks_per_seq;
+    a.num_blocks = num_blocks;
+    const long long rows = static_cast<long long>(num_tokens) * num_kv_heads;
+    kv_append_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    GK_CUDA(cudaGetLastError(), "kv_append_kernel launch");
+    return GOLLEK_OK;
+}
+
+int gollek_kv_migrate(const void *src_k, const void *src_v, void *dst_k, void *dst_v,
+                      const int *src_blocks, const int *dst_blocks, int num_copies,
+                      long long src_block_stride, long long dst_block_stride, long long bytes_per_block,
+                      int device, void *stream) {
+    t_last_error.clear();
+    if (!src_k || !dst_k || !src_blocks || !dst_blocks)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    if ((src_v == nullptr) != (dst_v == nullptr))
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "src_v and dst_v must both be set or both NULL");
+    if (num_copies < 0 || bytes_per_block < 0 || src_block_stride < 0 || dst_block_stride < 0)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "negative size");
+    if (num_copies == 0 || bytes_per_block == 0) return GOLLEK_OK;
+    DeviceGuard guard(device);
+    MigrateArgs a;
+    a.src[0] = static_cast<const uint8_t *>(src_k);
+    a.src[1] = static_cast<const uint8_t *>(src_v);
+    a.dst[0] = static_cast<uint8_t *>(dst_k);
+    a.dst[1] = static_cast<uint8_t *>(dst_v);
+    a.src_blocks = src_blocks;
+    a.dst_blocks = dst_blocks;
+    a.src_stride = src_block_stride;
+    a.dst_stride = dst_block_stride;
+    a.bytes = bytes_per_block;
+    a.tensors = src_v ? 2 : 1;
+    a.segs_per_block = (bytes_per_block + kSegBytes - 1) / kSegBytes;
+    a.num_units = static_cast<long long>(num_copies) * a.tensors * a.segs_per_block;
+    const bool vec = aligned16(src_k) && aligned16(dst_k) && (!src_v || (aligned16(src_v) && aligned16(dst_v))) &&
+                     bytes_per_block % 16 == 0 && src_block_stride % 16 == 0 && dst_block_stride % 16 == 0;
+    const long long grid = std::min<long long>(a.num_units, static_cast<long long>(sm_count(device)) * 4);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (vec)
+        kv_migrate_kernel_v16<<<static_cast<unsigned>(grid), 512, 0, st>>>(a);
+    else
+        kv_migrate_kernel_bytes<<<static_cast<unsigned>(grid), 256, 0, st>>>(a);
+    GK_CUDA(cudaGetLastError(), "kv_migrate launch");
+    return GOLLEK_OK;
+}
+
+int gollek_kv_block_checksum(const void *pool, const int *blocks, int n, long long block_stride,
+                             long long bytes_per_block, unsigned long long *checksums, void *stream) {
+    t_last_error.clear();
+    if (!pool || !blocks || !checksums) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    if (n < 0 || bytes_per_block % 8 != 0 || (reinterpret_cast<uintptr_t>(pool) & 7u) || block_stride % 8)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "checksums need 8-byte aligned blocks");
+    if (n == 0) return GOLLEK_OK;
+    block_checksum_kernel<<<n, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t *>(pool), blocks, block_stride, bytes_per_block, checksums);
+    GK_CUDA(cudaGetLastError(), "block_checksum_kernel launch");
+    return GOLLEK_OK;
+}
+
+int gollek_enable_peer_access(int device, int peer_device) {
+    t_last_error.clear();
+    if (device == peer_device) return GOLLEK_OK;
+    int can = 0;
+    GK_CUDA(cudaDeviceCanAccessPeer(&can, device, peer_device), "cudaDeviceCanAccessPeer");
+    if (!can) return fail(GOLLEK_ERR_UNSUPPORTED, "device %d cannot access device %d", device, peer_device);
+    DeviceGuard guard(device);
+    cudaError_t e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        return GOLLEK_OK;
+    }
+    GK_CUDA(e, "cudaDeviceEnablePeerAccess");
+    return GOLLEK_OK;
+}
+
+int gollek_ipc_get_handle(const void *dev_ptr, void *handle_out_64) {
+    t_last_error.clear();
+    if (!dev_ptr || !handle_out_64) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaIpcMemHandle_t h;
+    GK_CUDA(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)), "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    memcpy(handle_out_64, &h, sizeof(h));
+    return GOLLEK_OK;
+}
+
+int gollek_ipc_open_handle(const void *handle_64, void **dev_ptr_out) {
+    t_last_error.clear();
+    if (!handle_64 || !dev_ptr_out) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle_64, sizeof(h));
+    GK_CUDA(cudaIpcOpenMemHandle(dev_ptr_out, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    return GOLLEK_OK;
+}
+
+int gollek_ipc_close_handle(void *dev_ptr) {
+    t_last_error.clear();
+    if (!dev_ptr) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    GK_CUDA(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+    return GOLLEK_OK;
+}
+
+int gollek_device_status(int device, int clear, unsigned int *status_out) {
+    t_last_error.clear();
+    if (!status_out) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    if (gollek_cuda_device_count() == 0) return fail(GOLLEK_ERR_NO_DEVICE, "no CUDA device");
+    DeviceGuard guard(device);
+    GK_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    unsigned v = 0;
+    GK_CUDA(cudaMemcpyFromSymbol(&v, g_status, sizeof(v)), "read status");
+    if (clear) {
+        const unsigned zero = 0;
+        GK_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)), "clear status");
+    }
+    *status_out = v;
+    return GOLLEK_OK;
+}
+
+const char *gollek_last_error_string(void) { return t_last_error.c_str(); }
+
+const char *gollek_version(void) { return "gollek-b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

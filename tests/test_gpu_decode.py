@@ -1,0 +1,309 @@
+"""Parity of the CUDA decode-attention paths with the CPU oracle (through the C ABI).
+
+Tolerances: fp32 <= 1e-4 relative; bf16 / int8 KV <= 2e-2
+absolute against the fp32 oracle on the same rounded inputs.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import decode_case, oracle_decode, quantize_pages_int8, quantize_rows_int8
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _t(x, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def _fp32_close(got, want):
+    # <= 1e-4 relative, measured against the output's scale
+    err = np.abs(got - want).max()
+    ref = max(np.abs(want).max(), 1e-6)
+    assert err <= 1e-4 * ref, f"max err {err} vs scale {ref}"
+
+
+# ------------------------------------------------------------------ legacy ABI
+
+def test_legacy_config1_fp32(cuda_device):
+    """BASELINE config 1 through paged_attention_launch (fp32, MHA)."""
+    from gollek_b200 import ops
+    rng = np.random.default_rng(1)
+    ctx = np.array([37, 128, 301, 512], np.int32)
+    H, D, BS, NB = 8, 64, 16, 256
+    perm = rng.permutation(NB).astype(np.int32)
+    bt = np.zeros((4, 32), np.int32)
+    off = 0
+    for s, c in enumerate(ctx):
+        n = (c + BS - 1) // BS
+        bt[s, :n] = perm[off:off + n]
+        off += n
+    q = rng.standard_normal((4, H, D)).astype(np.float32)
+    k = rng.standard_normal((NB, H, BS, D)).astype(np.float32)
+    v = rng.standard_normal((NB, H, BS, D)).astype(np.float32)
+    scale = 1.0 / math.sqrt(D)
+    want = O.a1_execute(q, k, v, bt, ctx, scale)
+    out = torch.empty((4, H, D), dtype=torch.float32, device=cuda_device)
+    ops.paged_attention_launch(out, _t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                               _t(bt, cuda_device), _t(ctx, cuda_device), scale)
+    _fp32_close(out.cpu().numpy(), want)
+
+
+def test_legacy_reference_known_answers(cuda_device):
+    """PagedAttentionCpuFallbackTest.java:35-148 cases on the device (generic kernel)."""
+    from gollek_b200 import ops
+    q = np.array([[[1.0, 0.0]]], np.float32)
+    k = np.zeros((1, 1, 4, 2), np.float32)
+    k[0, 0, 0] = [1, 0]
+    k[0, 0, 1] = [0, 1]
+    out = torch.empty((1, 1, 2), device=cuda_device)
+    ops.paged_attention_launch(out, _t(q, cuda_device), _t(k, cuda_device), _t(k, cuda_device),
+                               _t(np.zeros((1, 1), np.int32), cuda_device),
+                               _t(np.array([2], np.int32), cuda_device), 1 / math.sqrt(2))
+    o = out.cpu().numpy()[0, 0]
+    assert o[0] > 0.5 and o[1] < 0.5 and abs(o.sum() - 1) < 1e-3
+
+    k2 = np.array([1, 1, 1, 0], np.float32).reshape(2, 1, 2, 1)
+    v2 = np.array([2, 4, 6, 0], np.float32).reshape(2, 1, 2, 1)
+    out = torch.empty((1, 1, 1), device=cuda_device)
+    ops.paged_attention_launch(out, _t(np.ones((1, 1, 1), np.float32), cuda_device),
+                               _t(k2, cuda_device), _t(v2, cuda_device),
+                               _t(np.array([[0, 1]], np.int32), cuda_device),
+                               _t(np.array([3], np.int32), cuda_device), 1.0)
+    assert abs(out.item() - 4.0) < 1e-3
+
+
+# ------------------------------------------------------------------ v2: bf16 GQA
+
+@pytest.mark.parametrize("hq,hkv,d,bs", [(32, 8, 128, 16), (8, 8, 128, 16), (16, 8, 128, 16),
+                                         (64, 8, 128, 16), (32, 8, 64, 16), (32, 8, 128, 8),
+                                         (32, 8, 128, 32), (32, 8, 128, 64)])
+def test_bf16_gqa_parity(cuda_device, hq, hkv, d, bs):
+    from gollek_b200 import ops
+    ctx = [1, 31, 32, 33, 200, 517, 1024, 2049, 0, 77]
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=d, bs=bs, seed=hq + d + bs, kv_std=0.5)
+    qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
+    scale = 1.0 / math.sqrt(d)
+    want = oracle_decode(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=bs)
+    out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kb, cuda_device, torch.bfloat16),
+                              _t(vb, cuda_device, torch.bfloat16), _t(bt, cuda_device),
+                              _t(ctx, cuda_device), num_kv_heads=hkv, block_size=bs, scale=scale,
+                              num_blocks=k.shape[0])
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    assert not got[8].any()  # empty context -> zeros
+
+
+@pytest.mark.parametrize("window,soft_cap", [(100, 0.0), (0, 30.0), (40, 5.0)])
+def test_window_and_softcap(cuda_device, window, soft_cap):
+    from gollek_b200 import ops
+    ctx = [1, 50, 129, 640, 1000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=5)
+    scale = 1.0 / math.sqrt(128)
+    want = oracle_decode(q, k, v, bt, ctx, scale, hkv=8, bs=16, soft_cap=soft_cap, window=window)
+    out = ops.paged_attention(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                              _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8,
+                              block_size=16, scale=scale, soft_cap=soft_cap, sliding_window=window,
+                              num_blocks=k.shape[0])
+    _fp32_close(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("hq,hkv,d,bs", [(32, 8, 128, 16), (8, 2, 64, 16), (4, 4, 64, 32)])
+def test_fp32_gqa_parity(cuda_device, hq, hkv, d, bs):
+    from gollek_b200 import ops
+    ctx = [3, 64, 300, 1500, 4100]
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=d, bs=bs, seed=11)
+    scale = 1.0 / math.sqrt(d)
+    want = oracle_decode(q, k, v, bt, ctx, scale, hkv=hkv, bs=bs)
+    out = ops.paged_attention(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                              _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=hkv,
+                              block_size=bs, scale=scale, num_blocks=k.shape[0])
+    _fp32_close(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("d,bs", [(5, 8), (2, 4), (96, 16), (128, 4)])
+def test_generic_shapes(cuda_device, d, bs):
+    """Shapes outside the TMA path go through the generic kernel."""
+    from gollek_b200 import ops
+    ctx = [1, 7, 40, 130]
+    q, k, v, bt, ctx = decode_case(ctx, hq=4, hkv=2, d=d, bs=bs, seed=d)
+    scale = 0.3
+    want = oracle_decode(q, k, v, bt, ctx, scale, hkv=2, bs=bs)
+    out = ops.paged_attention(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                              _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=2,
+                              block_size=bs, scale=scale, num_blocks=k.shape[0])
+    _fp32_close(out.cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ v2: int8 / int4
+
+def test_int8_reference_granularity(cuda_device):
+    """Per-(block, head, token) scales, the reference's BlockManager layout."""
+    from gollek_b200 import ops
+    ctx = [5, 100, 333, 1200, 2047]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=21, kv_std=0.5)
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    qb = O.round_bf16(q)
+    scale = 1.0 / math.sqrt(128)
+    want = oracle_decode(qb, kq, vq, bt, ctx, scale, hkv=8, bs=16, storage=O.INT8, k_scale=ks,
+                         v_scale=vs)
+    out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kq, cuda_device),
+                              _t(vq, cuda_device), _t(bt, cuda_device), _t(ctx, cuda_device),
+                              num_kv_heads=8, block_size=16, scale=scale, num_blocks=k.shape[0],
+                              k_scales=_t(ks, cuda_device), v_scales=_t(vs, cuda_device),
+                              scale_strides=(8 * 16, 16, 1))
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+def test_int8_page_granularity(cuda_device):
+    """one scale per (block, kv-head) from bf16 N(0, 0.5^2) values."""
+    from gollek_b200 import ops
+    ctx = [17, 512, 900, 3000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=22, kv_std=0.5)
+    k, v = O.round_bf16(k), O.round_bf16(v)
+    kq, ks = quantize_pages_int8(k)
+    vq, vs = quantize_pages_int8(v)
+    qb = O.round_bf16(q)
+    scale = 1.0 / math.sqrt(128)
+    ks_tok = np.repeat(ks[:, :, None], 16, axis=2)
+    vs_tok = np.repeat(vs[:, :, None], 16, axis=2)
+    want = oracle_decode(qb, kq, vq, bt, ctx, scale, hkv=8, bs=16, storage=O.INT8,
+                         k_scale=ks_tok, v_scale=vs_tok)
+    out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kq, cuda_device),
+                              _t(vq, cuda_device), _t(bt, cuda_device), _t(ctx, cuda_device),
+                              num_kv_heads=8, block_size=16, scale=scale, num_blocks=k.shape[0],
+                              k_scales=_t(ks, cuda_device), v_scales=_t(vs, cuda_device),
+                              scale_strides=(8, 1, 0))
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    # and against the fp32 oracle on the unquantised bf16 values (quantisation error)
+    want_f = oracle_decode(qb, k, v, bt, ctx, scale, hkv=8, bs=16)
+    assert np.abs(got - want_f).max() < 5e-2
+
+
+def test_int4_generic(cuda_device):
+    from gollek_b200 import ops
+    ctx = [3, 40, 200]
+    Hkv, D, BS = 2, 64, 16
+    q, k, v, bt, ctx = decode_case(ctx, hq=4, hkv=Hkv, d=D, bs=BS, seed=31)
+    nb = k.shape[0]
+    kq = np.zeros(nb * Hkv * BS * D // 2, np.uint8)
+    vq = np.zeros_like(kq)
+    ks = np.zeros(nb * Hkv * BS, np.float32)
+    vs = np.zeros_like(ks)
+    for r in range(nb * Hkv * BS):
+        O.write_vector(O.INT4, k.reshape(-1, D)[r], kq, r * D, ks, r)
+        O.write_vector(O.INT4, v.reshape(-1, D)[r], vq, r * D, vs, r)
+    scale = 0.125
+    want = oracle_decode(q, kq, vq, bt, ctx, scale, hkv=Hkv, bs=BS, storage=O.INT4, k_scale=ks,
+                         v_scale=vs)
+    out = ops.paged_attention(_t(q, cuda_device), _t(kq, cuda_device), _t(vq, cuda_device),
+                              _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=Hkv,
+                              block_size=BS, scale=scale, num_blocks=nb, k_scales=_t(ks, cuda_device),
+                              v_scales=_t(vs, cuda_device), scale_strides=(Hkv * BS, BS, 1),
+                              int4=True)
+    _fp32_close(out.cpu().numpy(), want)
+
+
+# ------------------------------------------------------------------ layouts, scratch, errors
+
+def test_physical_block_pool_layer_view(cuda_device):
+    """Attention on one layer of a [block][layer][H*BS*D] pool via base + page_stride."""
+    from gollek_b200 import ops
+    L, layer = 4, 2
+    ctx = [20, 300, 64]
+    q, k, v, bt, ctx = decode_case(ctx, hq=16, hkv=8, d=128, bs=16, seed=41)
+    nb = k.shape[0]
+    kp = np.random.default_rng(0).standard_normal((nb, L, 8, 16, 128)).astype(np.float32)
+    vp = np.random.default_rng(1).standard_normal((nb, L, 8, 16, 128)).astype(np.float32)
+    kp[:, layer], vp[:, layer] = k, v
+    kt, vt = _t(kp, cuda_device, torch.bfloat16), _t(vp, cuda_device, torch.bfloat16)
+    want = oracle_decode(O.round_bf16(q), O.round_bf16(k), O.round_bf16(v), bt, ctx,
+                         1 / math.sqrt(128), hkv=8, bs=16)
+    out = ops.paged_attention(_t(q, cuda_device, torch.bfloat16), kt[:, layer], vt[:, layer],
+                              _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8,
+                              block_size=16, num_blocks=nb, page_stride=L * 8 * 16 * 128)
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+def test_workspace_stays_zeroed_and_results_repeat(cuda_device):
+    from gollek_b200 import ops
+    ctx = [4000, 8000, 100, 5000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=51)
+    args = [_t(q, cuda_device, torch.bfloat16), _t(k, cuda_device, torch.bfloat16),
+            _t(v, cuda_device, torch.bfloat16), _t(bt, cuda_device), _t(ctx, cuda_device)]
+    ws = ops.new_workspace(4, 32, 8, 128, cuda_device)
+    outs = [ops.paged_attention(*args, num_kv_heads=8, block_size=16, num_blocks=k.shape[0],
+                                workspace=ws) for _ in range(3)]
+    lib_out = ops.paged_attention(*args, num_kv_heads=8, block_size=16, num_blocks=k.shape[0])
+    torch.cuda.synchronize()
+    nctr = 4 * 8
+    assert int(ws[: nctr * 4].view(torch.int32).abs().sum()) == 0
+    for o in outs[1:] + [lib_out]:
+        assert torch.equal(o, outs[0])
+
+
+def test_page_relocation_is_bit_exact(cuda_device):
+    """Moving pages in the pool (and remapping the table) leaves outputs bit-identical."""
+    from gollek_b200 import ops
+    ctx = [700, 3000, 9]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=61, spare_pages=40)
+    nb = k.shape[0]
+    perm = np.random.default_rng(7).permutation(nb)
+    inv = np.argsort(perm)
+    k2, v2 = k[perm], v[perm]                       # new page i holds old page perm[i]
+    bt2 = np.where(bt >= 0, inv[np.maximum(bt, 0)], -1).astype(np.int32)
+    run = lambda kk, vv, tt: ops.paged_attention(
+        _t(q, cuda_device, torch.bfloat16), _t(kk, cuda_device, torch.bfloat16),
+        _t(vv, cuda_device, torch.bfloat16), _t(tt, cuda_device), _t(ctx, cuda_device),
+        num_kv_heads=8, block_size=16, num_blocks=nb)
+    assert torch.equal(run(k, v, bt), run(k2, v2, bt2))
+
+
+def test_bad_block_id_reports_status(cuda_device):
+    from gollek_b200 import ops
+    from gollek_b200._lib import STATUS_BAD_BLOCK_ID
+    ctx = [40]
+    q, k, v, bt, ctx = decode_case(ctx, hq=8, hkv=8, d=128, bs=16, seed=71)
+    bt[0, 1] = k.shape[0] + 5  # outside the pool; the kernel must not read it
+    ops.device_status(cuda_device.index or 0, clear=True)
+    ops.paged_attention(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                        _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8, block_size=16,
+                        num_blocks=k.shape[0])
+    st = ops.device_status(cuda_device.index or 0, clear=True)
+    assert st & STATUS_BAD_BLOCK_ID
+    assert ops.device_status(cuda_device.index or 0) == 0
+
+
+def test_full_config2_sample_parity(cuda_device):
+    """BASELINE config 2 at full size; a seeded sample of sequences checked on the oracle."""
+    from gollek_b200 import ops
+    rng = np.random.default_rng(2024)
+    B, Hq, Hkv, D, BS = 64, 32, 8, 128, 16
+    ctx = rng.integers(512, 8193, B).astype(np.int32)
+    need = (ctx + BS - 1) // BS
+    nb = int(need.sum())
+    perm = rng.permutation(nb).astype(np.int32)
+    maxb = int(need.max())
+    bt = np.zeros((B, maxb), np.int32)
+    off = 0
+    for s in range(B):
+        bt[s, :need[s]] = perm[off:off + need[s]]
+        off += need[s]
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    k = (torch.randn((nb, Hkv, BS, D), generator=g, device=cuda_device) * 0.5).to(torch.bfloat16)
+    v = (torch.randn((nb, Hkv, BS, D), generator=g, device=cuda_device) * 0.5).to(torch.bfloat16)
+    q = torch.randn((B, Hq, D), generator=g, device=cuda_device).to(torch.bfloat16)
+    out = ops.paged_attention(q, k, v, _t(bt, cuda_device), _t(ctx, cuda_device),
+                              num_kv_heads=Hkv, block_size=BS, num_blocks=nb)
+    sample = [0, int(np.argmax(ctx)), int(np.argmin(ctx)), 33]
+    kf, vf = k.float().cpu().numpy(), v.float().cpu().numpy()
+    want = oracle_decode(q.float().cpu().numpy()[sample], kf, vf, bt[sample], ctx[sample],
+                         1 / math.sqrt(D), hkv=Hkv, bs=BS)
+    np.testing.assert_allclose(out.float().cpu().numpy()[sample], want, atol=2e-2, rtol=0)
