@@ -224,7 +224,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
     const int lane = tid & 31;
     const int S = a.num_seqs;
     const int Hkv = a.num_kv_heads;
-    const int NS = a.num_stages;
+    const int NS = a.num_stages;  // NC * SPW: consumer warp w owns stages [w*SPW, w*SPW+SPW)
+    const int SPW = NS / NC;
+    // Group gidx belongs to warp gidx % NC and lands in that warp's stage ring.  A stage
+    // is only ever waited on by its owner warp, in order, so no mbarrier wait is more
+    // than one phase ahead of the barrier (parity waits cannot alias).
+    auto stage_of = [&](int gi) { return (gi % NC) * SPW + (gi / NC) % SPW; };
+    auto round_of = [&](int gi) { return (gi / NC) / SPW; };
 
     // ------------------------------------------------------------ prologue
     if (tid == 0) {
@@ -337,8 +343,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
             int batch_base = -(1 << 30);
             int batch_entry = 0;  // lane i: block-table entry batch_base + i
             for (int g = g_beg; g < g_end; ++g, ++gidx) {
-                const int stage = gidx % NS;
-                const int round = gidx / NS;
+                const int stage = stage_of(gidx);
+                const int round = round_of(gidx);
                 if (round > 0) {
                     bool ok = true;
                     if (lane == 0) ok = mbar_wait(&empty_bar[stage], (round - 1) & 1);
@@ -408,7 +414,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
             // Let every copy already issued land before the CTA's shared memory is released.
             for (int k = 0; k < NS && k < gidx; ++k) {
                 const int gi = gidx - 1 - k;
-                if (lane == 0) mbar_wait(&full_bar[gi % NS], (gi / NS) & 1);
+                if (lane == 0) mbar_wait(&full_bar[stage_of(gi)], round_of(gi) & 1);
             }
         }
         return;
@@ -457,9 +463,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
         for (int g = g_beg; g < g_end; ++g, ++gidx) {
             if (gidx % NC != warp) continue;
             if (*cons_abort) continue;
-            const int stage = gidx % NS;
+            const int stage = stage_of(gidx);
             bool ok = true;
-            if (lane == 0) ok = mbar_wait(&full_bar[stage], (gidx / NS) & 1);
+            if (lane == 0) ok = mbar_wait(&full_bar[stage], round_of(gidx) & 1);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
                 *cons_abort = 1;

@@ -10,6 +10,8 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <tuple>
 #include <utility>
 
 #include "common.cuh"
@@ -79,7 +81,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 std::mutex g_mu;
 std::map<int, int> g_sm_count;
-std::map<std::pair<int, void *>, std::pair<void *, size_t>> g_ws;  // (device, stream) -> scratch
+// (device, stream, thread) -> scratch.  The thread is part of the key only for the
+// per-thread default stream, whose handle is the same constant on every thread.
+std::map<std::tuple<int, void *, size_t>, std::pair<void *, size_t>> g_ws;
 
 int sm_count(int dev) {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -93,8 +97,11 @@ int sm_count(int dev) {
 
 // Library-owned split-K scratch for (device, stream), zero-filled when (re)allocated.
 int library_workspace(int dev, void *stream, size_t bytes, void **out) {
+    const size_t tkey = stream == static_cast<void *>(cudaStreamPerThread)
+                            ? std::hash<std::thread::id>()(std::this_thread::get_id())
+                            : 0;
     std::lock_guard<std::mutex> lk(g_mu);
-    auto &slot = g_ws[{dev, stream}];
+    auto &slot = g_ws[std::make_tuple(dev, stream, tkey)];
     if (slot.second < bytes) {
         if (slot.first) {
             cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
@@ -137,8 +144,9 @@ size_t ws_bytes(int S, int Hq, int Hkv, int D) {
 
 // ------------------------------------------------------------------ fast path
 
-constexpr int kNC = 4;                  // consumer warps per CTA
+constexpr int kNC = 2;                  // consumer warps per CTA
 constexpr uint32_t kSmemBudget = 112 * 1024;  // per CTA: two CTAs share an SM's 228 KB
+constexpr int kMaxStagesPerWarp = 6;
 constexpr int kMinChunkGroups = 4;      // split-K chunk >= 128 tokens
 constexpr int kItemsPerCta = 4;
 
@@ -258,8 +266,10 @@ int run_v2(const V2 &p) {
         const bool quant = p.kv_dtype == GOLLEK_DTYPE_I8;
         const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * kSlabBytes;
         DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, kNC, 0, p.S);
-        int stages = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / (2 * tile));
-        stages = std::min(std::max(stages, 2), 16);
+        int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) /
+                                   (2 * tile * kNC));
+        spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
+        const int stages = spw * kNC;
         DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, kNC, stages, p.S);
         if (L.total > 227 * 1024) fn = nullptr;
         if (fn) {
