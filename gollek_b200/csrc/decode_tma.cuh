@@ -1,41 +1,52 @@
 // decode_tma.cuh -- persistent, warp-specialised paged decode attention for sm_100a.
 //
-// One CTA = NC consumer warps + 1 producer warp, resident for the whole launch
-// (grid = SMs x CTAs-per-SM).  The unit of work is an item (sequence, kv-head,
-// split-K chunk of 32-token groups).  Every CTA derives the same item list from
-// the context lengths in a prologue (a block-wide scan kept in shared memory) and
-// takes items b, b+grid, b+2*grid, ...
+// Work: the unit is a 16-token group of one (sequence, kv-head).  The prologue of
+// every CTA derives, from the context lengths, the linear order of all groups
+// (sequence-major, then kv-head, then position) and cuts it into gridDim.x equal
+// contiguous ranges (stream-K style): every CTA moves the same number of KV bytes,
+// whatever the length mix.  A range covers runs of consecutive groups of one
+// (sequence, kv-head); a run that does not cover its whole (sequence, kv-head) is a
+// split-K piece.
 //
-// Producer warp: for each 32-token group of its items, reads the block table,
-// and issues 2-D TMA tile loads (SWIZZLE_128B, no multicast) of the K and V rows
-// of the group's pages into a ring of shared-memory stages, completing on the
-// stage's mbarrier.  For int8 KV it also cp.async-copies the per-token scales.
+// One CTA = NC consumer warps + 1 producer warp, one CTA per SM.
+//   Producer: works in lane-parallel waves of up to 32 groups, one stage per lane:
+//   each lane reads its group's block-table entries, waits for its stage to be
+//   free and issues 2-D TMA tile loads (SWIZZLE_128B, no multicast) of the group's K
+//   and V rows, completing on the stage's mbarrier; int8 scales come by 4-byte
+//   cp.async.
+//   Consumer warp w owns a ring of SPW stages and takes groups w, w+NC, ... of the
+//   CTA's sequence of groups.  Owning its stages means a warp waits on each stage
+//   barrier in phase order, so parity waits cannot alias.
+//   Score pass: lane l handles token l%16 over head-dim half l/16 against the G
+//   query heads of the GQA group (q staged as fp32 in shared memory, broadcast
+//   reads), packed fp32x2 FMAs, halves joined by one shuffle.  Online softmax in the
+//   exp2 domain.  Value pass: lanes 0-15 take even rows and 16-31 odd rows, each lane
+//   owning head_dim/16 columns for all G heads.
+//   At a run's end the NC warp states merge through shared memory; a whole
+//   (sequence, kv-head) writes its output, a piece writes an fp32 partial (m, l, acc),
+//   and the CTA completing the last piece merges all of them (log-sum-exp) and
+//   resets the arrival counter, so the scratch stays zeroed between calls.
 //
-// Consumer warps: group j of an item goes to warp j % NC.  Score pass: lane z owns
-// token row z of the stage and dots it against the G query heads of the GQA group
-// (q staged in shared memory as fp32, read by broadcast), with packed fp32x2 FMAs.
-// Online softmax per head across the warp (exp2 domain).  Value pass: lanes 0-15
-// take even rows, 16-31 odd rows, each lane owning head_dim/16 columns of all G
-// heads.  At the end of an item the NC warp states merge through shared memory;
-// a single-chunk item writes the output, a multi-chunk item writes an fp32
-// partial (m, l, acc) and the CTA that completes the last chunk of a
-// (sequence, kv-head) merges all partials (split-K log-sum-exp reduce) and resets
-// the arrival counter, so the workspace stays zeroed between calls.
-//
-// The swizzled layout: each stage tile is stored as 128-byte-wide column slabs of
-// 32 rows; 16-byte chunk c of row r sits at chunk position c ^ (r & 7).  Lanes of a
-// quarter-warp read 8 different rows of the same logical chunk, or 8 chunks of one
-// row, and hit 8 distinct bank groups either way.
+// Stage layout: 128-byte-wide column slabs of 16 rows (2 KB); 16-byte chunk c of
+// row r sits at chunk position c ^ (r & 7), which is what TMA's 128-byte swizzle
+// writes.  The 8 lanes of a quarter-warp read 8 rows of one logical chunk, or 8
+// chunks of one row: 8 distinct bank groups either way.
 #pragma once
+
+#include <type_traits>
 
 #include "common.cuh"
 
 namespace gk {
 
-constexpr int kRows = 32;          // tokens per stage (one per lane in the score pass)
+constexpr int kRows = 16;          // tokens per stage
 constexpr int kSlabBytes = kRows * 128;
-constexpr int kMaxSplits = 64;     // split-K chunks per (sequence, kv-head) at most
+constexpr int kMaxSplits = 64;     // split-K pieces per (sequence, kv-head) at most
 constexpr int kMaxFastSeqs = 16384;
+constexpr int kMinRunGroups = 8;   // smallest per-CTA range, in groups
+// Cost of starting a run (a q load, a merge of the warp states, maybe a split-K
+// exchange), in 16-token groups; CTAs are balanced on groups + kRunCost per run.
+constexpr int kRunCost = 16;
 
 struct DecodeArgs {
     void *out;
@@ -44,16 +55,15 @@ struct DecodeArgs {
     const float *v_scales;
     const int *block_tables;
     const int *context_lens;
-    float *partials;   // split-K partial states: [slot][G*2 + G*D] fp32
+    float *partials;   // split-K partial states: [(s*Hkv+h)*kMaxSplits + piece][2G + G*D]
     int *counters;     // [num_seqs * num_kv_heads] arrival counters, zero between calls
     long long page_rows;  // rows of head_dim elements between consecutive pages
     long long scale_page_stride, scale_head_stride, scale_token_stride;
     int num_seqs, num_kv_heads, block_size, max_blocks, num_blocks;
     int window;           // <= 0: no sliding window
     int q_bf16;           // 1: q/out bf16, 0: fp32
-    int num_stages;
-    int min_chunk_groups;
-    int items_per_cta;
+    int num_stages;       // NC * stages per warp
+    int scale_mode;       // int8: 0 per-token scales by bulk copy, 1 one scale per page, 2 general
     float q_scale;        // applied to q when staged: scale*log2(e), or scale with soft-cap
     float soft_cap;       // > 0: cap*tanh(score/cap)
     float post_scale;     // log2(e) with soft-cap, else 1
@@ -119,10 +129,52 @@ __device__ __forceinline__ void decode_word<int8_t>(uint32_t w, float *f) {
     f[3] = b.y;
 }
 
+// Two floats -> one 32-bit register of the 16-bit MMA type (x0 in the low half).
+template <typename KV>
+__device__ __forceinline__ uint32_t pack2(float x0, float x1) {
+    if constexpr (std::is_same<KV, __half>::value) {
+        __half2 h = __floats2half2_rn(x0, x1);
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+template <typename KV>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+    if constexpr (std::is_same<KV, __half>::value)
+        return __half22float2(*reinterpret_cast<__half2 *>(&w));
+    else
+        return make_float2(bf16_lo(w), bf16_hi(w));
+}
+
+// c += A(16x16, row) * B(16x8, col) with fp32 accumulation.
+template <typename KV>
+__device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    if constexpr (std::is_same<KV, __half>::value)
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    else
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Byte offset in a swizzled stage tile of byte `b` of row `r`.
 __device__ __forceinline__ uint32_t swz(int r, int b) {
-    return static_cast<uint32_t>((b >> 7) * kSlabBytes + r * 128 + ((((b >> 4) & 7) ^ (r & 7)) << 4) +
-                                 (b & 15));
+    return static_cast<uint32_t>((b >> 7) * kSlabBytes + r * 128 +
+                                 ((((b >> 4) & 7) ^ (r & 7)) << 4) + (b & 15));
+}
+
+// q row layout in shared memory: each head's D floats with 4 floats of padding after
+// every 64, so the two head-dim halves of the score pass sit in different banks.
+__host__ __device__ constexpr int q_off(int D, int hh, int d) {
+    return hh * (D + 4 * (D / 64)) + d + 4 * (d / 64);
 }
 
 __device__ __forceinline__ void store_out(void *out, long long idx, float v, int bf16) {
@@ -134,29 +186,36 @@ __device__ __forceinline__ void store_out(void *out, long long idx, float v, int
 
 // Shared-memory carve-up, identical on host and device.
 struct DecodeSmem {
-    uint32_t stages, q, p, comb, scales, prefix, misc, bars, total;
+    uint32_t stages, q, p, comb, scales, prefix, cprefix, lens, rstart, misc, bars, total;
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
 __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quant, int D, int G,
-                                                         int NC, int stages, int num_seqs) {
+                                                         int NC, int stages, int num_seqs,
+                                                         int num_ctas) {
     DecodeSmem L;
     const uint32_t tile = static_cast<uint32_t>(D * kv_bytes / 128) * kSlabBytes;
     uint32_t o = 0;
     L.stages = o;
     o += stages * 2 * tile;
     L.q = o;
-    o += G * D * 4;
+    o += align_up(G * (D + 4 * (D / 64)) * 4, 16);
     L.p = o;
-    o += NC * kRows * G * 4;
+    o += NC * kRows * align_up(G, 4) * 4;
     L.comb = o;
     o += NC * G * (D + 2) * 4;
     L.scales = o;
     o += quant ? stages * 2 * kRows * 4 : 0;
     L.prefix = o;
     o += (num_seqs + 1) * 4;
+    L.cprefix = o;
+    o += (num_seqs + 1) * 4;
+    L.lens = o;
+    o += num_seqs * 4;
     o = align_up(o, 16);
+    L.rstart = o;
+    o += (num_ctas + 1) * 8;
     L.misc = o;
     o += 64;
     L.bars = o;
@@ -165,28 +224,27 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quan
     return L;
 }
 
-// Split-K plan of one sequence: its 32-token groups [g_lo, g_hi) in chunks of cs.
-struct SeqPlan {
-    int len, win_start, g_lo, n_groups, chunk;
+// Window of one sequence: groups [g_lo, g_lo + n) of 16 tokens cover [win_start, len).
+struct SeqWin {
+    int len, win_start, g_lo, n;
 };
 
-__device__ __forceinline__ SeqPlan seq_plan(const DecodeArgs &a, int s, int base_chunk) {
-    SeqPlan sp;
+__device__ __forceinline__ SeqWin seq_win(const DecodeArgs &a, int s) {
+    SeqWin w;
     int len = a.context_lens[s];
     const int cap = a.max_blocks * a.block_size;
-    if (len < 0) len = 0;
-    if (len > cap) len = cap;
-    sp.len = len;
-    sp.win_start = (a.window > 0 && len > a.window) ? len - a.window : 0;
-    sp.g_lo = sp.win_start / kRows;
-    sp.n_groups = len > 0 ? (len + kRows - 1) / kRows - sp.g_lo : 0;
-    const int need = (sp.n_groups + kMaxSplits - 1) / kMaxSplits;
-    sp.chunk = base_chunk > need ? base_chunk : need;
-    return sp;
+    len = len < 0 ? 0 : (len > cap ? cap : len);
+    w.len = len;
+    w.win_start = (a.window > 0 && len > a.window) ? len - a.window : 0;
+    w.g_lo = w.win_start / kRows;
+    w.n = len > 0 ? (len + kRows - 1) / kRows - w.g_lo : 0;
+    return w;
 }
 
-template <typename KV, int D, int G, int NC>
-__global__ void __launch_bounds__((NC + 1) * 32, 2)
+// SPLIT (16-bit KV only): q is wider than the MMA type (fp32 q, or any q with f16 KV)
+// and enters the score MMA as hi + lo halves.
+template <typename KV, int D, int G, int NC, bool SPLIT>
+__global__ void __launch_bounds__((NC + 1) * 32, 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
     constexpr int KB = KvType<KV>::kBytes;
@@ -194,27 +252,34 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
     constexpr int ROW_BYTES = D * KB;
     constexpr int NSLAB = ROW_BYTES / 128;
     constexpr int TILE = NSLAB * kSlabBytes;
-    constexpr int CH = ROW_BYTES / 16;     // 16-byte chunks per row
-    constexpr int EPC = 16 / KB;           // elements per chunk
-    constexpr int EPL = D / 16;            // value-pass columns per lane
-    constexpr int LANE_BYTES = EPL * KB;   // value-pass bytes per lane per row
+    constexpr int HALF_CH = ROW_BYTES / 32;  // 16-byte chunks per head-dim half
+    constexpr int EPC = 16 / KB;             // elements per chunk
+    constexpr int EPW = 4 / KB;              // elements per 32-bit word
+    constexpr int EPL = D / 16;              // value-pass columns per lane
+    constexpr int LANE_BYTES = EPL * KB;     // value-pass bytes per lane per row
+    constexpr int GP = (G + 3) / 4 * 4;      // p row stride (floats)
+    constexpr int QROW = D + 4 * (D / 64);
     constexpr int NT = (NC + 1) * 32;
     constexpr int CONS = NC * 32;
-    constexpr int EPW = 4 / KB;            // elements per 32-bit word
     static_assert(ROW_BYTES % 128 == 0, "row must be a whole number of 128-byte slabs");
-    static_assert(EPL % 2 == 0 && EPC % 4 == 0, "vector widths");
-    static_assert(NSLAB * 2 * 4 <= 32, "TMA loads of one group (<= 4 pages) fit a warp");
+    static_assert(EPL % 2 == 0 && EPC % 4 == 0 && D % 64 == 0, "vector widths");
+    static_assert(NSLAB * 2 * 2 <= 32, "TMA loads of one stage (<= 2 pages) fit a warp");
 
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const DecodeSmem L = decode_smem_layout(KB, QUANT, D, G, NC, a.num_stages, a.num_seqs);
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    // Align to 1024 bytes by pointer arithmetic on the shared array (keeps the
+    // shared address space visible to the compiler).
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const DecodeSmem L =
+        decode_smem_layout(KB, QUANT, D, G, NC, a.num_stages, a.num_seqs, gridDim.x);
     uint8_t *sm_stage = smem + L.stages;
     float *sm_q = reinterpret_cast<float *>(smem + L.q);
     float *sm_p = reinterpret_cast<float *>(smem + L.p);
     float *sm_comb = reinterpret_cast<float *>(smem + L.comb);
     float *sm_scale = reinterpret_cast<float *>(smem + L.scales);
     int *sm_prefix = reinterpret_cast<int *>(smem + L.prefix);
+    int *sm_cprefix = reinterpret_cast<int *>(smem + L.cprefix);  // per-sequence cost prefix
+    int *sm_len = reinterpret_cast<int *>(smem + L.lens);  // context lengths, clamped to the table
+    long long *sm_rstart = reinterpret_cast<long long *>(smem + L.rstart);  // CTA range starts
     volatile int *sm_misc = reinterpret_cast<volatile int *>(smem + L.misc);
     uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *empty_bar = full_bar + a.num_stages;
@@ -224,24 +289,21 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
     const int lane = tid & 31;
     const int S = a.num_seqs;
     const int Hkv = a.num_kv_heads;
-    const int NS = a.num_stages;  // NC * SPW: consumer warp w owns stages [w*SPW, w*SPW+SPW)
+    const int NS = a.num_stages;
     const int SPW = NS / NC;
-    // Group gidx belongs to warp gidx % NC and lands in that warp's stage ring.  A stage
-    // is only ever waited on by its owner warp, in order, so no mbarrier wait is more
-    // than one phase ahead of the barrier (parity waits cannot alias).
     auto stage_of = [&](int gi) { return (gi % NC) * SPW + (gi / NC) % SPW; };
     auto round_of = [&](int gi) { return (gi / NC) / SPW; };
 
     // ------------------------------------------------------------ prologue
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
-            mbar_init(&full_bar[i], QUANT ? 1 + 32 : 1);
+            mbar_init(&full_bar[i], (QUANT && a.scale_mode != 0) ? 2 : 1);
             mbar_init(&empty_bar[i], 1);
         }
         fence_barrier_init();
-        sm_misc[0] = 0;  // abort flag
-        sm_misc[1] = 0;  // "this CTA merges the partials" flag
-        sm_misc[2] = 0;  // total groups (reduction)
+        sm_misc[0] = 0;  // "this CTA merges the partials" flag
+        sm_misc[1] = 0;  // max groups of one sequence (reduction)
+        sm_misc[3] = 0;  // consumer abort flag
     }
     if (warp == NC && lane == 0) {
         prefetch_tensormap(&tm_k);
@@ -249,364 +311,733 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
     }
     __syncthreads();
 
-    // Total groups over all sequences -> uniform chunk size.
-    int my_groups = 0;
-    for (int s = tid; s < S; s += NT) {
-        my_groups += seq_plan(a, s, 1).n_groups;
-        const int raw = a.context_lens[s];
-        if (raw < 0 || raw > a.max_blocks * a.block_size) raise_status(GOLLEK_STATUS_BAD_POSITION);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) my_groups += __shfl_xor_sync(0xffffffffu, my_groups, o);
-    if (lane == 0) atomicAdd(const_cast<int *>(&sm_misc[2]), my_groups);
-    __syncthreads();
-    const long long total_units = static_cast<long long>(sm_misc[2]) * Hkv;
-    const long long target = static_cast<long long>(gridDim.x) * a.items_per_cta;
-    int base_chunk = static_cast<int>((total_units + target - 1) / (target > 0 ? target : 1));
-    if (base_chunk < a.min_chunk_groups) base_chunk = a.min_chunk_groups;
-    if (base_chunk < 1) base_chunk = 1;
-
-    // Exclusive prefix over per-sequence split counts (contiguous segment per thread).
+    // Exclusive prefix of per-sequence group counts (contiguous segment per thread).
     {
         const int seg = (S + NT - 1) / NT;
-        const int s0 = tid * seg;
+        const int s0 = min(S, tid * seg);
         const int s1 = min(S, s0 + seg);
-        int sum = 0;
+        int sum = 0, csum = 0, mx = 0;
         for (int s = s0; s < s1; ++s) {
-            SeqPlan sp = seq_plan(a, s, base_chunk);
-            int splits = sp.n_groups > 0 ? (sp.n_groups + sp.chunk - 1) / sp.chunk : 1;
-            sm_prefix[s] = splits;
-            sum += splits;
+            const int raw = a.context_lens[s];
+            if (raw < 0 || raw > a.max_blocks * a.block_size) raise_status(GOLLEK_STATUS_BAD_POSITION);
+            const SeqWin w0 = seq_win(a, s);
+            sm_len[s] = w0.len;
+            const int n = w0.n;
+            sm_prefix[s] = n;
+            sm_cprefix[s] = n > 0 ? n + kRunCost : 0;
+            sum += n;
+            csum += n > 0 ? n + kRunCost : 0;
+            mx = max(mx, n);
         }
-        // inclusive warp scan of per-thread sums
-        int incl = sum;
+        int incl = sum, cincl = csum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            const int cv = __shfl_up_sync(0xffffffffu, cincl, o);
+            if (lane >= o) {
+                incl += v;
+                cincl += cv;
+            }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         int *warp_tot = reinterpret_cast<int *>(sm_comb);  // scratch before first use
-        if (lane == 31) warp_tot[warp] = incl;
+        int *warp_ctot = warp_tot + 32;
+        if (lane == 31) {
+            warp_tot[warp] = incl;
+            warp_ctot[warp] = cincl;
+        }
+        if (lane == 0) atomicMax(const_cast<int *>(&sm_misc[1]), mx);
         __syncthreads();
         if (tid == 0) {
-            int run = 0;
+            int run = 0, crun = 0;
             for (int w = 0; w <= NC; ++w) {
-                int t = warp_tot[w];
+                const int t = warp_tot[w], ct = warp_ctot[w];
                 warp_tot[w] = run;
+                warp_ctot[w] = crun;
                 run += t;
+                crun += ct;
             }
             sm_prefix[S] = run;
+            sm_cprefix[S] = crun;
         }
         __syncthreads();
         int run = warp_tot[warp] + incl - sum;
+        int crun = warp_ctot[warp] + cincl - csum;
         for (int s = s0; s < s1; ++s) {
-            int v = sm_prefix[s];
+            const int v = sm_prefix[s], cv = sm_cprefix[s];
             sm_prefix[s] = run;
+            sm_cprefix[s] = crun;
             run += v;
+            crun += cv;
         }
         __syncthreads();
     }
-    const int num_items = sm_prefix[S] * Hkv;
-
-    // Item -> (sequence, kv-head, chunk).
-    auto locate = [&](int item, int &s, int &h, int &c) {
-        const int u = item / Hkv;
-        h = item - u * Hkv;
+    // Linear group space: unit x = (prefix[s] * Hkv) + h * n_s + g.  CTA ranges are cut
+    // in cost space, where each (sequence, kv-head) costs its groups plus kRunCost, so
+    // a CTA that starts many runs gets fewer groups.  Ranges stay contiguous in x.
+    const long long total = static_cast<long long>(sm_prefix[S]) * Hkv;
+    const long long tcost = static_cast<long long>(sm_cprefix[S]) * Hkv;
+    const int max_n = sm_misc[1];
+    long long per_cost = (tcost + gridDim.x - 1) / gridDim.x;
+    const long long per_floor = (max_n + kMaxSplits - 3) / (kMaxSplits - 2);
+    if (per_cost < per_floor) per_cost = per_floor;
+    if (per_cost < kMinRunGroups) per_cost = kMinRunGroups;
+    const int g_eff = static_cast<int>(min(static_cast<long long>(gridDim.x),
+                                           (tcost + per_cost - 1) / per_cost));
+    // group position where cost c falls (the run's first group for cost inside its
+    // start-up share)
+    auto x_of_cost = [&](long long c) -> long long {
+        if (c >= tcost) return total;
         int lo = 0, hi = S - 1;
         while (lo < hi) {
-            int mid = (lo + hi + 1) >> 1;
-            if (sm_prefix[mid] <= u)
+            const int mid = (lo + hi + 1) >> 1;
+            if (static_cast<long long>(sm_cprefix[mid]) * Hkv <= c)
                 lo = mid;
             else
                 hi = mid - 1;
         }
-        s = lo;
-        c = u - sm_prefix[lo];
+        const int n = sm_prefix[lo + 1] - sm_prefix[lo];
+        const int m = n + kRunCost;
+        const int y = static_cast<int>(c - static_cast<long long>(sm_cprefix[lo]) * Hkv);
+        const int h = y / m;
+        const int v = y - h * m;
+        return static_cast<long long>(sm_prefix[lo]) * Hkv + static_cast<long long>(h) * n +
+               (v > kRunCost ? v - kRunCost : 0);
+    };
+    // range starts of all CTAs, computed once
+    for (int b = tid; b <= static_cast<int>(gridDim.x); b += NT)
+        sm_rstart[b] = b >= g_eff ? total : x_of_cost(static_cast<long long>(b) * per_cost);
+    __syncthreads();
+    // the CTA whose range holds group x: the last b with range_start(b) <= x
+    auto owner = [&](long long x) -> int {
+        int lo = 0, hi = g_eff - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (sm_rstart[mid] <= x)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        return lo;
+    };
+    const long long x_beg = sm_rstart[blockIdx.x];
+    const long long x_end = sm_rstart[blockIdx.x + 1];
+
+    // Run containing unit x: sequence s, kv-head h, group offset g within the window,
+    // the run's length and the piece index / piece count of (s, h).
+    struct Run {
+        int s, h, g, len, piece, pieces;
+        long long sh_start, sh_end;
+    };
+    auto run_at = [&](long long x) {
+        Run r;
+        int lo = 0, hi = S - 1;
+        while (lo < hi) {  // last s with prefix[s]*Hkv <= x
+            const int mid = (lo + hi + 1) >> 1;
+            if (static_cast<long long>(sm_prefix[mid]) * Hkv <= x)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        r.s = lo;
+        const int n = sm_prefix[lo + 1] - sm_prefix[lo];  // > 0: x lies inside sequence lo
+        const int y = static_cast<int>(x - static_cast<long long>(sm_prefix[lo]) * Hkv);
+        r.h = y / n;
+        r.g = y - r.h * n;
+        const long long sh_start =
+            static_cast<long long>(sm_prefix[lo]) * Hkv + static_cast<long long>(r.h) * n;
+        const long long sh_end = sh_start + n;
+        r.len = static_cast<int>(min(sh_end, x_end) - x);
+        r.sh_start = sh_start;
+        r.sh_end = sh_end;
+        return r;
+    };
+    // split-K piece index of this CTA's run and the piece count of its (s, h)
+    auto run_pieces = [&](Run &r) {
+        const int first = owner(r.sh_start);
+        r.piece = static_cast<int>(blockIdx.x) - first;
+        r.pieces = owner(r.sh_end - 1) - first + 1;
     };
 
     if (warp == NC) {
         // ========================================================= producer
-        // Pages of one group: BS < 32 -> 32/BS whole pages (R = BS rows each);
-        // BS >= 32 -> one 32-row slice of a page.
-        const int R = a.block_size < kRows ? a.block_size : kRows;
-        const int npg = kRows / R;  // <= 4 (BS >= 8)
-        int gidx = 0;
+        // Lane-parallel waves: lane i of a wave owns CTA-local group gbase + i, one
+        // stage per lane (wave size <= number of stages).  Each lane waits for its own
+        // stage to be free and issues its own TMA loads, without waiting for the other
+        // lanes.  The next wave's page ids are looked up (block-table loads in flight)
+        // while the current wave waits and issues, so a wave starts with its ids ready.
+        const int R = a.block_size < kRows ? a.block_size : kRows;  // rows per TMA box
+        const int npg = kRows / R;                                  // pages per stage (<= 2)
+        const int W = NS < 32 ? NS : 32;
+        struct GroupLoc {
+            int h, t0, row_off, pid0, pid1, stage, round, len, win_start;
+            unsigned loaded;
+        };
+        auto locate_group = [&](long long x, int gi) {
+            GroupLoc q;
+            const Run r = run_at(x);
+            const int len = sm_len[r.s];
+            q.len = len;
+            q.win_start = (a.window > 0 && len > a.window) ? len - a.window : 0;
+            q.h = r.h;
+            q.stage = stage_of(gi);
+            q.round = round_of(gi);
+            q.t0 = (q.win_start / kRows + r.g) * kRows;
+            const int p_first = q.t0 / a.block_size;
+            q.row_off = a.block_size < kRows ? 0 : q.t0 % a.block_size;
+            const int pages_in_seq = (len + a.block_size - 1) / a.block_size;
+            const int *bt = a.block_tables + static_cast<long long>(r.s) * a.max_blocks;
+            q.pid0 = q.pid1 = 0;
+            q.loaded = 0;
+            for (int j = 0; j < npg; ++j) {
+                const int pg = p_first + j;
+                if (pg < pages_in_seq && (pg + 1) * a.block_size > q.win_start) {
+                    const int e = __ldg(bt + pg);
+                    if (j)
+                        q.pid1 = e;
+                    else
+                        q.pid0 = e;
+                    q.loaded |= 1u << j;
+                }
+            }
+            return q;
+        };
+        auto checked = [&](int e) {
+            if (e < 0 || (a.num_blocks > 0 && e >= a.num_blocks)) {
+                raise_status(GOLLEK_STATUS_BAD_BLOCK_ID);
+                return 0;
+            }
+            return e;
+        };
+        int gbase = 0;
         bool aborted = false;
-        for (int item = blockIdx.x; item < num_items && !aborted; item += gridDim.x) {
-            int s, h, c;
-            locate(item, s, h, c);
-            const SeqPlan sp = seq_plan(a, s, base_chunk);
-            const int g_beg = sp.g_lo + c * sp.chunk;
-            const int g_end = min(sp.g_lo + sp.n_groups, g_beg + sp.chunk);
-            const int *bt = a.block_tables + static_cast<long long>(s) * a.max_blocks;
-            const int pages_in_seq = (sp.len + a.block_size - 1) / a.block_size;
-            int batch_base = -(1 << 30);
-            int batch_entry = 0;  // lane i: block-table entry batch_base + i
-            for (int g = g_beg; g < g_end; ++g, ++gidx) {
-                const int stage = stage_of(gidx);
-                const int round = round_of(gidx);
-                if (round > 0) {
-                    bool ok = true;
-                    if (lane == 0) ok = mbar_wait(&empty_bar[stage], (round - 1) & 1);
-                    ok = __shfl_sync(0xffffffffu, ok, 0);
-                    if (!ok) {
-                        aborted = true;
-                        break;
-                    }
-                }
-                const int t0 = g * kRows;
-                const int p_first = t0 / a.block_size;
-                const int row_off = a.block_size < kRows ? 0 : t0 % a.block_size;
-                if (p_first < batch_base || p_first + npg - 1 >= batch_base + 32) {
-                    batch_base = p_first;
-                    const int e = batch_base + lane;
-                    batch_entry = (e < pages_in_seq) ? __ldg(bt + e) : 0;
-                }
-                // lane j < npg resolves page j of the group
-                const int pg = p_first + lane;
-                const bool need = lane < npg && pg < pages_in_seq &&
-                                  (pg + 1) * a.block_size > sp.win_start;
-                int entry = __shfl_sync(0xffffffffu, batch_entry, (pg - batch_base) & 31);
-                if (need && (entry < 0 || (a.num_blocks > 0 && entry >= a.num_blocks))) {
-                    raise_status(GOLLEK_STATUS_BAD_BLOCK_ID);
-                    entry = 0;
-                }
-                const unsigned loaded = __ballot_sync(0xffffffffu, need);
+        long long xw = x_beg;
+        int nw = static_cast<int>(min(static_cast<long long>(W), x_end - xw));
+        GroupLoc cur{};
+        if (lane < nw) cur = locate_group(xw + lane, gbase + lane);
+        while (xw < x_end) {
+            // look up the next wave while this one waits and issues
+            const long long xn = xw + nw;
+            const int gn = gbase + nw;
+            const int nw_next = static_cast<int>(min(static_cast<long long>(W), x_end - xn));
+            GroupLoc nxt{};
+            if (lane < nw_next) nxt = locate_group(xn + lane, gn + lane);
+
+            const bool act = lane < nw;
+            bool ok = true;
+            if (act && cur.round > 0) ok = mbar_wait(&empty_bar[cur.stage], (cur.round - 1) & 1);
+            if (act && ok) {
+                const int stage = cur.stage;
+                const int pid0 = checked(cur.pid0), pid1 = checked(cur.pid1);
+                const unsigned loaded = cur.loaded;
                 uint8_t *kdst = sm_stage + static_cast<uint32_t>(stage) * 2 * TILE;
                 uint8_t *vdst = kdst + TILE;
-                if (lane == 0)
-                    mbar_arrive_expect_tx(&full_bar[stage],
-                                          static_cast<uint32_t>(__popc(loaded)) * 2u * NSLAB * R * 128u);
-                __syncwarp();
-                // one lane per (page, slab, K/V) TMA load: npg * NSLAB * 2 <= 32
-                {
-                    const int j = lane / (NSLAB * 2);
-                    const int rem = lane - j * NSLAB * 2;
-                    const int pj = __shfl_sync(0xffffffffu, entry, j & 31);
-                    if (j < npg && ((loaded >> j) & 1)) {
-                        const int slab = rem >> 1;
-                        const int isv = rem & 1;
-                        const long long y = static_cast<long long>(pj) * a.page_rows +
-                                            static_cast<long long>(h) * a.block_size + row_off;
-                        uint8_t *dst = (isv ? vdst : kdst) + slab * kSlabBytes + j * R * 128;
-                        tma_load_2d(dst, isv ? &tm_v : &tm_k, slab * (128 / KB),
+                const uint32_t scale_tx = (QUANT && a.scale_mode == 0) ? 2u * R * 4u : 0u;
+                mbar_arrive_expect_tx(&full_bar[stage], static_cast<uint32_t>(__popc(loaded)) *
+                                                            (2u * NSLAB * R * 128u + scale_tx));
+                for (int j = 0; j < npg; ++j) {
+                    if (!((loaded >> j) & 1)) continue;
+                    const long long y = static_cast<long long>(j ? pid1 : pid0) * a.page_rows +
+                                        static_cast<long long>(cur.h) * a.block_size + cur.row_off;
+#pragma unroll
+                    for (int slab = 0; slab < NSLAB; ++slab) {
+                        tma_load_2d(kdst + slab * kSlabBytes + j * R * 128, &tm_k, slab * (128 / KB),
+                                    static_cast<int>(y), &full_bar[stage]);
+                        tma_load_2d(vdst + slab * kSlabBytes + j * R * 128, &tm_v, slab * (128 / KB),
                                     static_cast<int>(y), &full_bar[stage]);
                     }
                 }
                 if constexpr (QUANT) {
-                    const int t = t0 + lane;
-                    const int j = lane / R;
-                    const int pj = __shfl_sync(0xffffffffu, entry, j);
                     float *ks = sm_scale + stage * 2 * kRows;
-                    if (t >= sp.win_start && t < sp.len && ((loaded >> j) & 1)) {
-                        const long long so =
-                            static_cast<long long>(pj) * a.scale_page_stride +
-                            static_cast<long long>(h) * a.scale_head_stride +
-                            static_cast<long long>(t % a.block_size) * a.scale_token_stride;
-                        cp_async_4(ks + lane, a.k_scales + so);
-                        cp_async_4(ks + kRows + lane, a.v_scales + so);
+                    if (a.scale_mode == 0) {
+                        // per-token scales: R contiguous floats per page, one bulk copy each
+                        for (int j = 0; j < npg; ++j) {
+                            if (!((loaded >> j) & 1)) continue;
+                            const long long so =
+                                static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
+                                static_cast<long long>(cur.h) * a.scale_head_stride + cur.row_off;
+                            bulk_load(ks + j * R, a.k_scales + so, R * 4u, &full_bar[stage]);
+                            bulk_load(ks + kRows + j * R, a.v_scales + so, R * 4u, &full_bar[stage]);
+                        }
+                    } else if (a.scale_mode == 1) {
+                        // one scale per (page, kv-head): slot j of the stage
+                        for (int j = 0; j < npg; ++j) {
+                            if (!((loaded >> j) & 1)) continue;
+                            const long long so =
+                                static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
+                                static_cast<long long>(cur.h) * a.scale_head_stride;
+                            cp_async_4(ks + j, a.k_scales + so);
+                            cp_async_4(ks + kRows + j, a.v_scales + so);
+                        }
+                        cp_async_mbar_arrive_noinc(&full_bar[stage]);
+                    } else {
+                        for (int tk = 0; tk < kRows; ++tk) {
+                            const int t = cur.t0 + tk;
+                            const int j = tk / R;
+                            if (t >= cur.win_start && t < cur.len && ((loaded >> j) & 1)) {
+                                const long long so =
+                                    static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
+                                    static_cast<long long>(cur.h) * a.scale_head_stride +
+                                    static_cast<long long>(t % a.block_size) * a.scale_token_stride;
+                                cp_async_4(ks + tk, a.k_scales + so);
+                                cp_async_4(ks + kRows + tk, a.v_scales + so);
+                            }
+                        }
+                        cp_async_mbar_arrive_noinc(&full_bar[stage]);
                     }
-                    cp_async_mbar_arrive_noinc(&full_bar[stage]);
                 }
+            }
+            xw = xn;
+            gbase = gn;
+            nw = nw_next;
+            cur = nxt;
+            if (!__all_sync(0xffffffffu, ok)) {
+                aborted = true;
+                break;
             }
         }
         if (aborted) {
             // Let every copy already issued land before the CTA's shared memory is released.
-            for (int k = 0; k < NS && k < gidx; ++k) {
-                const int gi = gidx - 1 - k;
-                if (lane == 0) mbar_wait(&full_bar[stage_of(gi)], round_of(gi) & 1);
+            const int k = lane;
+            if (k < NS && k < gbase) {
+                const int g = gbase - 1 - k;
+                mbar_wait(&full_bar[stage_of(g)], round_of(g) & 1);
             }
         }
         return;
     }
 
     // ============================================================ consumers
-    // Control flow below depends only on state the consumer warps themselves write
-    // before a named barrier, so all NC warps take the same barriers.
+    // Control flow below depends only on state the consumer warps write before a
+    // named barrier, so all NC warps take the same barriers.
     const int half = lane >> 4;
     const int li = lane & 15;
-    float *my_p = sm_p + warp * kRows * G;
+    // int8 scale slot of token li of a stage: per token, or per page (scale_mode 1)
+    const int scale_slot =
+        a.scale_mode == 1 ? li / (a.block_size < kRows ? a.block_size : kRows) : li;
+    const uint32_t p_base = smem_u32(sm_p) + warp * kRows * GP * 4;
     volatile int *cons_abort = sm_misc + 3;
-    if (tid == 0) *cons_abort = 0;
-    named_barrier(1, CONS);
-    int gidx = 0;
-    for (int item = blockIdx.x; item < num_items; item += gridDim.x) {
-        int s, h, c;
-        locate(item, s, h, c);
-        const SeqPlan sp = seq_plan(a, s, base_chunk);
-        const int g_beg = sp.g_lo + c * sp.chunk;
-        const int g_end = min(sp.g_lo + sp.n_groups, g_beg + sp.chunk);
-        const int splits = sm_prefix[s + 1] - sm_prefix[s];
 
-        // Stage q (G heads of this kv-head's group), scaled, as fp32.
-        {
-            const long long qbase = (static_cast<long long>(s) * Hkv + h) * G * D;
-            for (int i = tid; i < G * D; i += CONS) {
-                float v = a.q_bf16 ? __bfloat162float(
-                                         reinterpret_cast<const __nv_bfloat16 *>(a.q)[qbase + i])
-                                   : reinterpret_cast<const float *>(a.q)[qbase + i];
-                sm_q[i] = v * a.q_scale;
-            }
-        }
-        named_barrier(1, CONS);
+    // Sequences with nothing to attend to: zeros, written by CTA s % grid.
+    for (int s = blockIdx.x; s < S; s += gridDim.x) {
+        if (sm_prefix[s + 1] != sm_prefix[s]) continue;
+        for (int o = tid; o < Hkv * G * D; o += CONS)
+            store_out(a.out, static_cast<long long>(s) * Hkv * G * D + o, 0.f, a.q_bf16);
+    }
 
-        float m[G], l[G];
-        float2 acc[G][EPL / 2];
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-            m[hh] = -INFINITY;
-            l[hh] = 0.f;
-#pragma unroll
-            for (int e = 0; e < EPL / 2; ++e) acc[hh][e] = make_float2(0.f, 0.f);
-        }
+    // bf16 q with bf16 KV: q's words are the score MMA's A fragments as they are, so the
+    // next run's q can be loaded into registers while the current run merges.
+    constexpr bool kQPrefetch = std::is_same<KV, __nv_bfloat16>::value && !SPLIT;
+    uint32_t qnext[kQPrefetch ? D / 16 : 1][2];
+    bool have_qnext = false;
+    int gidx = 0;        // CTA-local index of the run's first group
+    int my_slot = 0;     // this warp's next stage (of SPW) and its phase parity
+    uint32_t my_phase = 0;
+    for (long long x = x_beg; x < x_end;) {
+        Run r = run_at(x);
+        run_pieces(r);
+        x += r.len;
+        SeqWin sw;
+        sw.len = sm_len[r.s];
+        sw.win_start = (a.window > 0 && sw.len > a.window) ? sw.len - a.window : 0;
+        sw.g_lo = sw.win_start / kRows;
+        sw.n = sm_prefix[r.s + 1] - sm_prefix[r.s];
 
-        for (int g = g_beg; g < g_end; ++g, ++gidx) {
-            if (gidx % NC != warp) continue;
-            if (*cons_abort) continue;
-            const int stage = stage_of(gidx);
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(&full_bar[stage], round_of(gidx) & 1);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) {
-                *cons_abort = 1;
-                continue;
-            }
-            const uint8_t *kt = sm_stage + static_cast<uint32_t>(stage) * 2 * TILE;
-            const uint8_t *vt = kt + TILE;
-            const int t0 = g * kRows;
-            const int v_lo = max(sp.win_start - t0, 0);
-            const int v_hi = min(sp.len - t0, kRows);
-
-            // ---------------- score pass: lane = token row
-            float sc[G];
-            {
-                float2 dot[G];
+        if constexpr (KB == 2) {
+            // ======== 16-bit KV: dot products on the tensor pipe (mma.sync m16n8k16,
+            // fp32 accumulate).  Scores S = Q K^T with the G heads as rows (padded to
+            // 16); values O^T = V^T P^T with head_dim as rows, the heads as the 8
+            // columns, so the probabilities go from the score accumulators straight
+            // into the B operand.
+            constexpr int KS = D / 16;  // k-steps of the score MMA = m-tiles of the value MMA
+            const int g = lane >> 2;    // fragment row group
+            const int t = lane & 3;     // fragment column pair
+            // q as A fragments (row g = head g; rows g+8 are zero), split hi + lo when the
+            // input is wider than the MMA type so the scores stay fp32-accurate.
+            uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
+            if (kQPrefetch && have_qnext) {
 #pragma unroll
-                for (int hh = 0; hh < G; ++hh) dot[hh] = make_float2(0.f, 0.f);
-#pragma unroll 2
-                for (int ch = 0; ch < CH; ++ch) {
-                    const uint4 raw = *reinterpret_cast<const uint4 *>(kt + swz(lane, ch * 16));
-                    float kf[EPC];
-                    decode_word<KV>(raw.x, kf + 0 * EPW);
-                    decode_word<KV>(raw.y, kf + 1 * EPW);
-                    decode_word<KV>(raw.z, kf + 2 * EPW);
-                    decode_word<KV>(raw.w, kf + 3 * EPW);
+                for (int kk = 0; kk < KS; ++kk) {
+                    qa[kk][0] = qnext[kk][0];
+                    qa[kk][1] = qnext[kk][1];
+                }
+            } else {
+                const long long qrow = ((static_cast<long long>(r.s) * Hkv + r.h) * G + g) * D;
 #pragma unroll
-                    for (int hh = 0; hh < G; ++hh) {
+                for (int kk = 0; kk < KS; ++kk) {
 #pragma unroll
-                        for (int e = 0; e < EPC; e += 4) {
-                            const float4 qv =
-                                *reinterpret_cast<const float4 *>(sm_q + hh * D + ch * EPC + e);
-                            dot[hh] = __ffma2_rn(make_float2(qv.x, qv.y),
-                                                 make_float2(kf[e], kf[e + 1]), dot[hh]);
-                            dot[hh] = __ffma2_rn(make_float2(qv.z, qv.w),
-                                                 make_float2(kf[e + 2], kf[e + 3]), dot[hh]);
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const int d = 16 * kk + 2 * t + 8 * hf;
+                        float x0 = 0.f, x1 = 0.f;
+                        if (g < G) {
+                            if (a.q_bf16) {
+                                const __nv_bfloat162 v2 =
+                                    *reinterpret_cast<const __nv_bfloat162 *>(
+                                        reinterpret_cast<const __nv_bfloat16 *>(a.q) + qrow + d);
+                                x0 = __low2float(v2);
+                                x1 = __high2float(v2);
+                            } else {
+                                const float2 v2 = *reinterpret_cast<const float2 *>(
+                                    reinterpret_cast<const float *>(a.q) + qrow + d);
+                                x0 = v2.x;
+                                x1 = v2.y;
+                            }
+                        }
+                        qa[kk][hf] = pack2<KV>(x0, x1);
+                        if constexpr (SPLIT) {
+                            const float2 back = unpack2<KV>(qa[kk][hf]);
+                            ql[kk][hf] = pack2<KV>(x0 - back.x, x1 - back.y);
                         }
                     }
                 }
-                const bool valid = lane >= v_lo && lane < v_hi;
-                float kscale = 1.f;
-                if constexpr (QUANT) kscale = sm_scale[stage * 2 * kRows + lane];
-#pragma unroll
-                for (int hh = 0; hh < G; ++hh) {
-                    float x = (dot[hh].x + dot[hh].y) * kscale;
-                    if (a.soft_cap > 0.f) x = a.soft_cap * tanhf(x / a.soft_cap) * a.post_scale;
-                    sc[hh] = valid ? x : -INFINITY;
-                }
             }
+            float m_run = -INFINITY;  // running max of head g (quad-uniform)
+            float l_run = 0.f;        // this lane's share of head g's normaliser
+            float o[KS][4];           // O^T fragments: d = 16*mt + g (+8), heads 2t, 2t+1
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+            // ldmatrix row address of lane: token r + 8*(i>>1), 8 columns at 8*(i&1)
+            const int lm_tok = (lane & 7) + 8 * (lane >> 4);
+            const int lm_col = 8 * ((lane >> 3) & 1);
 
-            // ---------------- online softmax (exp2 domain), per head across the warp
-            bool rescale = false;
-            float alpha[G];
-            float vscale = 1.f;
-            if constexpr (QUANT) vscale = sm_scale[stage * 2 * kRows + kRows + lane];
-#pragma unroll
-            for (int hh = 0; hh < G; ++hh) {
-                const float mx = warp_max(sc[hh]);
-                const float mn = fmaxf(m[hh], mx);
-                alpha[hh] = (mn == m[hh]) ? 1.f : fast_exp2(m[hh] - mn);
-                rescale |= (mn != m[hh]);
-                m[hh] = mn;
-                const float mref = (mn == -INFINITY) ? 0.f : mn;
-                const float p = fast_exp2(sc[hh] - mref);
-                l[hh] = l[hh] * alpha[hh] + p;
-                my_p[lane * G + hh] = p * vscale;
-            }
-            if (rescale) {
-#pragma unroll
-                for (int hh = 0; hh < G; ++hh) {
-                    const float2 al = make_float2(alpha[hh], alpha[hh]);
-#pragma unroll
-                    for (int e = 0; e < EPL / 2; ++e) acc[hh][e] = __fmul2_rn(acc[hh][e], al);
+            for (int j = ((warp - gidx) % NC + NC) % NC; j < r.len; j += NC) {
+                if (*cons_abort) continue;
+                const int stage = warp * SPW + my_slot;
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (++my_slot == SPW) {
+                    my_slot = 0;
+                    my_phase ^= 1;
                 }
-            }
-            __syncwarp();
-
-            // ---------------- value pass: lanes 0-15 even rows, 16-31 odd rows
-            for (int r = v_lo + half; r < v_hi; r += 2) {
-                float vf[EPL];
-                const int b0 = li * LANE_BYTES;
-                if constexpr (LANE_BYTES >= 16) {
-#pragma unroll
-                    for (int k = 0; k < LANE_BYTES / 16; ++k) {
-                        const uint4 raw = *reinterpret_cast<const uint4 *>(vt + swz(r, b0 + 16 * k));
-                        decode_word<KV>(raw.x, vf + (4 * k + 0) * EPW);
-                        decode_word<KV>(raw.y, vf + (4 * k + 1) * EPW);
-                        decode_word<KV>(raw.z, vf + (4 * k + 2) * EPW);
-                        decode_word<KV>(raw.w, vf + (4 * k + 3) * EPW);
+                if (!ok) {
+                    *cons_abort = 1;
+                    continue;
+                }
+                const uint32_t kt = smem_u32(sm_stage) + static_cast<uint32_t>(stage) * 2 * TILE;
+                const uint32_t vt = kt + TILE;
+                const int t0 = (sw.g_lo + r.g + j) * kRows;
+                const int v_lo = max(sw.win_start - t0, 0);
+                const int v_hi = min(sw.len - t0, kRows);
+                if (v_lo > 0 || v_hi < kRows) {
+                    // Rows outside the window may hold anything (NaN included) and a zero
+                    // probability does not cancel a NaN on the tensor pipe: clear them.
+                    constexpr int CHR = ROW_BYTES / 16;
+                    for (int idx = lane; idx < kRows * CHR; idx += 32) {
+                        const int rr = idx / CHR;
+                        if (rr < v_lo || rr >= v_hi)
+                            sts_u4(vt + swz(rr, (idx - rr * CHR) * 16), make_uint4(0, 0, 0, 0));
                     }
-                } else {
-                    static_assert(LANE_BYTES == 8 || LANE_BYTES >= 16, "value-pass width");
-                    const uint2 raw = *reinterpret_cast<const uint2 *>(vt + swz(r, b0));
-                    decode_word<KV>(raw.x, vf + 0 * EPW);
-                    decode_word<KV>(raw.y, vf + 1 * EPW);
+                    __syncwarp();
                 }
-                float pv[G];
-                if constexpr (G % 4 == 0) {
+                // ---------------- K and V fragments to registers, then free the stage at
+                // once: the producer refills it while this warp computes.
+                uint32_t kb[KS][4], vb[KS][4];
 #pragma unroll
-                    for (int hh = 0; hh < G; hh += 4) {
-                        const float4 t = *reinterpret_cast<const float4 *>(my_p + r * G + hh);
+                for (int kk = 0; kk < KS; ++kk) {
+                    ldsm_x4(kt + swz(lm_tok, (16 * kk + lm_col) * 2), kb[kk]);
+                    ldsm_x4_trans(vt + swz(lm_tok, (16 * kk + lm_col) * 2), vb[kk]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_bar[stage]);
+                // ---------------- scores (two accumulator chains per n-tile)
+                float s[2][4], s2[2][4];
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[nt][e] = s2[nt][e] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    float(*acc)[4] = (kk & 1) ? s2 : s;
+                    mma_16816<KV>(acc[0], qa[kk][0], 0u, qa[kk][1], 0u, kb[kk][0], kb[kk][1]);
+                    mma_16816<KV>(acc[1], qa[kk][0], 0u, qa[kk][1], 0u, kb[kk][2], kb[kk][3]);
+                    if constexpr (SPLIT) {
+                        mma_16816<KV>(acc[0], ql[kk][0], 0u, ql[kk][1], 0u, kb[kk][0], kb[kk][1]);
+                        mma_16816<KV>(acc[1], ql[kk][0], 0u, ql[kk][1], 0u, kb[kk][2], kb[kk][3]);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
+                // ---------------- online softmax for head g over tokens 8nt + 2t + e
+                float p[2][2];
+                float mloc = -INFINITY;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int tk = 8 * nt + 2 * t + e;
+                        float x2 = s[nt][e];
+                        if (a.soft_cap > 0.f) {
+                            x2 *= a.q_scale;
+                            x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
+                        } else {
+                            x2 *= a.q_scale;
+                        }
+                        x2 = (tk >= v_lo && tk < v_hi) ? x2 : -INFINITY;
+                        p[nt][e] = x2;
+                        mloc = fmaxf(mloc, x2);
+                    }
+                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+                const float mn = fmaxf(m_run, mloc);
+                const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
+                const float mref = (mn == -INFINITY) ? 0.f : mn;
+                m_run = mn;
+                float psum = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        p[nt][e] = fast_exp2(p[nt][e] - mref);
+                        psum += p[nt][e];
+                    }
+                l_run = l_run * alpha + psum;
+                const uint32_t pb0 = pack2<KV>(p[0][0], p[0][1]);
+                const uint32_t pb1 = pack2<KV>(p[1][0], p[1][1]);
+                if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * t);      // head 2t
+                    const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * t + 4);  // head 2t+1
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        o[mt][0] *= al0;
+                        o[mt][1] *= al1;
+                        o[mt][2] *= al0;
+                        o[mt][3] *= al1;
+                    }
+                }
+                // ---------------- values
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt)
+                    mma_16816<KV>(o[mt], vb[mt][0], vb[mt][1], vb[mt][2], vb[mt][3], pb0, pb1);
+            }
+            gidx += r.len;
+
+            // ---------------- next run's q, in flight while this run merges
+            if constexpr (kQPrefetch) {
+                have_qnext = x < x_end;
+                if (have_qnext) {
+                    const Run rn = run_at(x);
+                    const uint32_t *qw = reinterpret_cast<const uint32_t *>(a.q) +
+                                         ((static_cast<long long>(rn.s) * Hkv + rn.h) * G + g) * (D / 2);
+#pragma unroll
+                    for (int kk = 0; kk < KS; ++kk) {
+                        qnext[kk][0] = g < G ? __ldg(qw + 8 * kk + t) : 0u;
+                        qnext[kk][1] = g < G ? __ldg(qw + 8 * kk + 4 + t) : 0u;
+                    }
+                }
+            }
+            // ---------------- this warp's state -> shared memory
+            float *cw = sm_comb + warp * G * (D + 2);
+            l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+            l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+            if (t == 0 && g < G) {
+                cw[g] = m_run;
+                cw[G + g] = l_run;
+            }
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                const int d0 = 16 * mt + g;
+                if (2 * t < G) {
+                    cw[2 * G + (2 * t) * D + d0] = o[mt][0];
+                    cw[2 * G + (2 * t) * D + d0 + 8] = o[mt][2];
+                }
+                if (2 * t + 1 < G) {
+                    cw[2 * G + (2 * t + 1) * D + d0] = o[mt][1];
+                    cw[2 * G + (2 * t + 1) * D + d0 + 8] = o[mt][3];
+                }
+            }
+        } else {
+            // Stage q (G heads of this kv-head's group), scaled, as fp32.
+            {
+                const long long qbase = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
+                for (int i = tid; i < G * D; i += CONS) {
+                    const float v = a.q_bf16
+                                        ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.q)[qbase + i])
+                                        : reinterpret_cast<const float *>(a.q)[qbase + i];
+                    sm_q[q_off(D, i / D, i % D)] = v * a.q_scale;
+                }
+            }
+            named_barrier(1, CONS);
+
+            float m[G], l[G];
+            float2 acc[G][EPL / 2];
+    #pragma unroll
+            for (int hh = 0; hh < G; ++hh) {
+                m[hh] = -INFINITY;
+                l[hh] = 0.f;
+    #pragma unroll
+                for (int e = 0; e < EPL / 2; ++e) acc[hh][e] = make_float2(0.f, 0.f);
+            }
+
+            // this warp's groups of the run: CTA-local indices gidx + j with (gidx + j) % NC == warp
+            for (int j = ((warp - gidx) % NC + NC) % NC; j < r.len; j += NC) {
+                if (*cons_abort) continue;
+                const int stage = warp * SPW + my_slot;
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (++my_slot == SPW) {
+                    my_slot = 0;
+                    my_phase ^= 1;
+                }
+                if (!ok) {
+                    *cons_abort = 1;
+                    continue;
+                }
+                const uint32_t kt = smem_u32(sm_stage) + static_cast<uint32_t>(stage) * 2 * TILE;
+                const uint32_t vt = kt + TILE;
+                const int t0 = (sw.g_lo + r.g + j) * kRows;
+                const int v_lo = max(sw.win_start - t0, 0);
+                const int v_hi = min(sw.len - t0, kRows);
+
+                // ---------------- score pass: lane = (token li, head-dim half)
+                float sc[G];
+                {
+                    float2 dot[G];
+    #pragma unroll
+                    for (int hh = 0; hh < G; ++hh) dot[hh] = make_float2(0.f, 0.f);
+                    const uint32_t qh = smem_u32(sm_q) + q_off(D, 0, half * (D / 2)) * 4;
+    #pragma unroll
+                    for (int ch = 0; ch < HALF_CH; ++ch) {
+                        const uint4 raw = lds_u4(kt + swz(li, (half * HALF_CH + ch) * 16));
+                        float kf[EPC];
+                        decode_word<KV>(raw.x, kf + 0 * EPW);
+                        decode_word<KV>(raw.y, kf + 1 * EPW);
+                        decode_word<KV>(raw.z, kf + 2 * EPW);
+                        decode_word<KV>(raw.w, kf + 3 * EPW);
+    #pragma unroll
+                        for (int hh = 0; hh < G; ++hh) {
+    #pragma unroll
+                            for (int e = 0; e < EPC; e += 4) {
+                                const float4 qv = lds_f4(qh + (hh * QROW + ch * EPC + e) * 4);
+                                dot[hh] = __ffma2_rn(make_float2(qv.x, qv.y),
+                                                     make_float2(kf[e], kf[e + 1]), dot[hh]);
+                                dot[hh] = __ffma2_rn(make_float2(qv.z, qv.w),
+                                                     make_float2(kf[e + 2], kf[e + 3]), dot[hh]);
+                            }
+                        }
+                    }
+                    const bool valid = li >= v_lo && li < v_hi;
+                    float kscale = 1.f;
+                    if constexpr (QUANT) kscale = sm_scale[stage * 2 * kRows + scale_slot];
+    #pragma unroll
+                    for (int hh = 0; hh < G; ++hh) {
+                        float x2 = dot[hh].x + dot[hh].y;
+                        x2 += __shfl_xor_sync(0xffffffffu, x2, 16);
+                        x2 *= kscale;
+                        if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
+                        sc[hh] = valid ? x2 : -INFINITY;
+                    }
+                }
+
+                // ---------------- online softmax (exp2 domain), per head over the 16 tokens
+                bool rescale = false;
+                float alpha[G], pw[GP];
+                float vscale = 1.f;
+                if constexpr (QUANT) vscale = sm_scale[stage * 2 * kRows + kRows + scale_slot];
+    #pragma unroll
+                for (int hh = 0; hh < G; ++hh) {
+                    float mx = sc[hh];
+    #pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    const float mn = fmaxf(m[hh], mx);
+                    alpha[hh] = (mn == m[hh]) ? 1.f : fast_exp2(m[hh] - mn);
+                    rescale |= (mn != m[hh]);
+                    m[hh] = mn;
+                    const float mref = (mn == -INFINITY) ? 0.f : mn;
+                    const float p = fast_exp2(sc[hh] - mref);
+                    l[hh] = l[hh] * alpha[hh] + (half == 0 ? p : 0.f);
+                    pw[hh] = p * vscale;
+                }
+    #pragma unroll
+                for (int hh = G; hh < GP; ++hh) pw[hh] = 0.f;
+                if (half == 0) {
+    #pragma unroll
+                    for (int hh = 0; hh < GP; hh += 4)
+                        sts_f4(p_base + (li * GP + hh) * 4,
+                               make_float4(pw[hh], pw[hh + 1], pw[hh + 2], pw[hh + 3]));
+                }
+                if (rescale) {
+    #pragma unroll
+                    for (int hh = 0; hh < G; ++hh) {
+                        const float2 al = make_float2(alpha[hh], alpha[hh]);
+    #pragma unroll
+                        for (int e = 0; e < EPL / 2; ++e) acc[hh][e] = __fmul2_rn(acc[hh][e], al);
+                    }
+                }
+                __syncwarp();
+
+                // ---------------- value pass: lanes 0-15 even rows, 16-31 odd rows
+                auto value_row = [&](int rr) {
+                    float vf[EPL];
+                    const int b0 = li * LANE_BYTES;
+                    if constexpr (LANE_BYTES >= 16) {
+    #pragma unroll
+                        for (int k = 0; k < LANE_BYTES / 16; ++k) {
+                            const uint4 raw = lds_u4(vt + swz(rr, b0 + 16 * k));
+                            decode_word<KV>(raw.x, vf + (4 * k + 0) * EPW);
+                            decode_word<KV>(raw.y, vf + (4 * k + 1) * EPW);
+                            decode_word<KV>(raw.z, vf + (4 * k + 2) * EPW);
+                            decode_word<KV>(raw.w, vf + (4 * k + 3) * EPW);
+                        }
+                    } else {
+                        static_assert(LANE_BYTES == 8 || LANE_BYTES >= 16, "value-pass width");
+                        const uint2 raw = lds_u2(vt + swz(rr, b0));
+                        decode_word<KV>(raw.x, vf + 0 * EPW);
+                        decode_word<KV>(raw.y, vf + 1 * EPW);
+                    }
+                    float pv[GP];
+    #pragma unroll
+                    for (int hh = 0; hh < GP; hh += 4) {
+                        const float4 t = lds_f4(p_base + (rr * GP + hh) * 4);
                         pv[hh] = t.x;
                         pv[hh + 1] = t.y;
                         pv[hh + 2] = t.z;
                         pv[hh + 3] = t.w;
                     }
+    #pragma unroll
+                    for (int hh = 0; hh < G; ++hh) {
+                        const float2 pp = make_float2(pv[hh], pv[hh]);
+    #pragma unroll
+                        for (int e = 0; e < EPL / 2; ++e)
+                            acc[hh][e] = __ffma2_rn(pp, make_float2(vf[2 * e], vf[2 * e + 1]), acc[hh][e]);
+                    }
+                };
+                if (v_lo == 0 && v_hi == kRows) {  // a full group: fixed trip count, unrolled
+    #pragma unroll
+                    for (int i = 0; i < kRows / 2; ++i) value_row(2 * i + half);
                 } else {
-#pragma unroll
-                    for (int hh = 0; hh < G; ++hh) pv[hh] = my_p[r * G + hh];
+                    for (int rr = v_lo + half; rr < v_hi; rr += 2) value_row(rr);
                 }
-#pragma unroll
-                for (int hh = 0; hh < G; ++hh) {
-                    const float2 pp = make_float2(pv[hh], pv[hh]);
-#pragma unroll
-                    for (int e = 0; e < EPL / 2; ++e)
-                        acc[hh][e] = __ffma2_rn(pp, make_float2(vf[2 * e], vf[2 * e + 1]), acc[hh][e]);
-                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_bar[stage]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty_bar[stage]);
-        }
+            gidx += r.len;
 
-        // ---------------- merge the NC warp states of this item
-        {
-            float *cw = sm_comb + warp * G * (D + 2);
-#pragma unroll
-            for (int hh = 0; hh < G; ++hh) {
-                const float lw = warp_sum(l[hh]);
-#pragma unroll
-                for (int e = 0; e < EPL / 2; ++e) {
-                    acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
-                    acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
-                }
-                if (lane == 0) {
-                    cw[hh] = m[hh];
-                    cw[G + hh] = lw;
-                }
-                if (half == 0) {
-#pragma unroll
+            // ---------------- merge the NC warp states of this run
+            {
+                float *cw = sm_comb + warp * G * (D + 2);
+    #pragma unroll
+                for (int hh = 0; hh < G; ++hh) {
+                    const float lw = warp_sum(l[hh]);
+    #pragma unroll
                     for (int e = 0; e < EPL / 2; ++e) {
-                        cw[2 * G + hh * D + li * EPL + 2 * e] = acc[hh][e].x;
-                        cw[2 * G + hh * D + li * EPL + 2 * e + 1] = acc[hh][e].y;
+                        acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
+                        acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
+                    }
+                    if (lane == 0) {
+                        cw[hh] = m[hh];
+                        cw[G + hh] = lw;
+                    }
+                    if (half == 0) {
+    #pragma unroll
+                        for (int e = 0; e < EPL / 2; ++e) {
+                            cw[2 * G + hh * D + li * EPL + 2 * e] = acc[hh][e].x;
+                            cw[2 * G + hh * D + li * EPL + 2 * e + 1] = acc[hh][e].y;
+                        }
                     }
                 }
             }
@@ -614,12 +1045,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
         named_barrier(1, CONS);
         if (*cons_abort) break;  // a wait gave up in this CTA: stop cleanly
 
-        const long long out_row = (static_cast<long long>(s) * Hkv + h) * G * D;
+        const long long out_row = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
         const int slot_floats = 2 * G + G * D;
         float *part = nullptr;
-        if (splits > 1)
+        if (r.pieces > 1)
             part = a.partials +
-                   (static_cast<long long>(sm_prefix[s] + c) * Hkv + h) * slot_floats;
+                   (static_cast<long long>(r.s * Hkv + r.h) * kMaxSplits + r.piece) * slot_floats;
         for (int o = tid; o < G * D; o += CONS) {
             const int hh = o / D;
             float M = -INFINITY;
@@ -636,7 +1067,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
                     As += cw[2 * G + o] * f;
                 }
             }
-            if (splits == 1) {
+            if (r.pieces == 1) {
                 const float v = Ls > 0.f ? As * (1.0f / (Ls + a.norm_eps)) : 0.f;
                 store_out(a.out, out_row + o, v, a.q_bf16);
             } else {
@@ -647,27 +1078,26 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
                 }
             }
         }
-        if (splits > 1) {
+        if (r.pieces > 1) {
             __threadfence();
             named_barrier(1, CONS);
             if (tid == 0) {
-                const int old = atomicAdd(&a.counters[s * Hkv + h], 1);
-                sm_misc[1] = (old == splits - 1) ? 1 : 0;
+                const int old = atomicAdd(&a.counters[r.s * Hkv + r.h], 1);
+                sm_misc[0] = (old == r.pieces - 1) ? 1 : 0;
             }
             named_barrier(1, CONS);
-            if (sm_misc[1]) {
+            if (sm_misc[0]) {
                 __threadfence();
-                const float *base = a.partials +
-                                    (static_cast<long long>(sm_prefix[s]) * Hkv + h) * slot_floats;
-                const long long step = static_cast<long long>(Hkv) * slot_floats;
+                const float *base =
+                    a.partials + static_cast<long long>(r.s * Hkv + r.h) * kMaxSplits * slot_floats;
                 for (int o = tid; o < G * D; o += CONS) {
                     const int hh = o / D;
                     float M = -INFINITY;
-                    for (int cc = 0; cc < splits; ++cc) M = fmaxf(M, __ldcg(base + cc * step + hh));
+                    for (int c = 0; c < r.pieces; ++c) M = fmaxf(M, __ldcg(base + c * slot_floats + hh));
                     float Ls = 0.f, As = 0.f;
                     if (M != -INFINITY) {
-                        for (int cc = 0; cc < splits; ++cc) {
-                            const float *pc = base + cc * step;
+                        for (int c = 0; c < r.pieces; ++c) {
+                            const float *pc = base + c * slot_floats;
                             const float mc = __ldcg(pc + hh);
                             const float f = (mc == -INFINITY) ? 0.f : fast_exp2(mc - M);
                             Ls += __ldcg(pc + G + hh) * f;
@@ -677,7 +1107,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 2)
                     const float v = Ls > 0.f ? As * (1.0f / (Ls + a.norm_eps)) : 0.f;
                     store_out(a.out, out_row + o, v, a.q_bf16);
                 }
-                if (tid == 0) atomicExch(&a.counters[s * Hkv + h], 0);
+                if (tid == 0) atomicExch(&a.counters[r.s * Hkv + r.h], 0);
             }
         }
     }

@@ -144,11 +144,9 @@ size_t ws_bytes(int S, int Hq, int Hkv, int D) {
 
 // ------------------------------------------------------------------ fast path
 
-constexpr int kNC = 2;                  // consumer warps per CTA
-constexpr uint32_t kSmemBudget = 112 * 1024;  // per CTA: two CTAs share an SM's 228 KB
+constexpr int kNC = 8;                  // consumer warps per CTA (one CTA per SM)
+constexpr uint32_t kSmemBudget = 224 * 1024;
 constexpr int kMaxStagesPerWarp = 6;
-constexpr int kMinChunkGroups = 4;      // split-K chunk >= 128 tokens
-constexpr int kItemsPerCta = 4;
 
 struct Launch {
     const void *fn;
@@ -156,32 +154,38 @@ struct Launch {
     bool quant;
 };
 
-template <typename KV, int D, int G>
+template <typename KV, int D, int G, bool SPLIT>
 const void *fast_kernel() {
-    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, kNC>);
+    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, kNC, SPLIT>);
 }
 
-template <typename KV, int D>
+template <typename KV, int D, bool SPLIT>
 const void *pick_g(int G) {
     switch (G) {
-        case 1: return fast_kernel<KV, D, 1>();
-        case 2: return fast_kernel<KV, D, 2>();
-        case 4: return fast_kernel<KV, D, 4>();
-        case 8: return fast_kernel<KV, D, 8>();
+        case 1: return fast_kernel<KV, D, 1, SPLIT>();
+        case 2: return fast_kernel<KV, D, 2, SPLIT>();
+        case 4: return fast_kernel<KV, D, 4, SPLIT>();
+        case 8: return fast_kernel<KV, D, 8, SPLIT>();
         default: return nullptr;
     }
 }
 
-const void *pick_fast(int kv, int D, int G) {
+// 16-bit KV computes on the tensor pipe; q wider than the MMA type (fp32 q, or any q
+// with f16 KV) is split into hi + lo halves (SPLIT).
+const void *pick_fast(int kv, int D, int G, bool q_f32) {
     switch (kv) {
         case GOLLEK_DTYPE_BF16:
-            return D == 128 ? pick_g<__nv_bfloat16, 128>(G) : D == 64 ? pick_g<__nv_bfloat16, 64>(G) : nullptr;
+            if (q_f32)
+                return D == 128 ? pick_g<__nv_bfloat16, 128, true>(G)
+                                : D == 64 ? pick_g<__nv_bfloat16, 64, true>(G) : nullptr;
+            return D == 128 ? pick_g<__nv_bfloat16, 128, false>(G)
+                            : D == 64 ? pick_g<__nv_bfloat16, 64, false>(G) : nullptr;
         case GOLLEK_DTYPE_F16:
-            return D == 128 ? pick_g<__half, 128>(G) : D == 64 ? pick_g<__half, 64>(G) : nullptr;
+            return D == 128 ? pick_g<__half, 128, true>(G) : D == 64 ? pick_g<__half, 64, true>(G) : nullptr;
         case GOLLEK_DTYPE_F32:
-            return D == 128 ? pick_g<float, 128>(G) : D == 64 ? pick_g<float, 64>(G) : nullptr;
+            return D == 128 ? pick_g<float, 128, false>(G) : D == 64 ? pick_g<float, 64, false>(G) : nullptr;
         case GOLLEK_DTYPE_I8:
-            return D == 128 ? pick_g<int8_t, 128>(G) : nullptr;
+            return D == 128 ? pick_g<int8_t, 128, false>(G) : nullptr;
         default:
             return nullptr;
     }
@@ -234,7 +238,7 @@ int encode_map(CUtensorMap *m, const void *base, int kv, int D, long long rows, 
 const void *fast_eligible(const V2 &p, int G, long long page_stride) {
     const int eb = dtype_bytes(p.kv_dtype);
     if (eb == 0) return nullptr;
-    const void *fn = pick_fast(p.kv_dtype, p.D, G);
+    const void *fn = pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32);
     if (!fn) return nullptr;
     const bool bs_ok = (p.BS >= 8 && p.BS <= 32 && 32 % p.BS == 0) || (p.BS > 32 && p.BS % 32 == 0);
     if (!bs_ok) return nullptr;
@@ -265,12 +269,13 @@ int run_v2(const V2 &p) {
         const int eb = dtype_bytes(p.kv_dtype);
         const bool quant = p.kv_dtype == GOLLEK_DTYPE_I8;
         const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * kSlabBytes;
-        DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, kNC, 0, p.S);
+        const int max_ctas = sm_count(dev) * 2;
+        DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, kNC, 0, p.S, max_ctas);
         int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) /
                                    (2 * tile * kNC));
         spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
         const int stages = spw * kNC;
-        DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, kNC, stages, p.S);
+        DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, kNC, stages, p.S, max_ctas);
         if (L.total > 227 * 1024) fn = nullptr;
         if (fn) {
             void *ws = p.workspace;
@@ -313,8 +318,15 @@ int run_v2(const V2 &p) {
             a.window = p.window;
             a.q_bf16 = p.q_dtype == GOLLEK_DTYPE_BF16;
             a.num_stages = stages;
-            a.min_chunk_groups = kMinChunkGroups;
-            a.items_per_cta = kItemsPerCta;
+            a.scale_mode = 2;
+            if (quant) {
+                const int R = p.BS < kRows ? p.BS : kRows;
+                if (p.sts == 1 && (p.sps * 4) % 16 == 0 && (p.shs * 4) % 16 == 0 && aligned16(p.ks) &&
+                    aligned16(p.vs) && (R * 4) % 16 == 0)
+                    a.scale_mode = 0;
+                else if (p.sts == 0)
+                    a.scale_mode = 1;
+            }
             a.q_scale = cap ? p.scale : p.scale * log2e;
             a.soft_cap = p.soft_cap;
             a.post_scale = cap ? log2e : 1.f;
@@ -326,7 +338,7 @@ int run_v2(const V2 &p) {
             GK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, (kNC + 1) * 32, L.total),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
             if (per_sm < 1) per_sm = 1;
-            const int grid = sm_count(dev) * per_sm;
+            const int grid = std::min(sm_count(dev) * per_sm, max_ctas);  // smem sized for max_ctas
             void *args[] = {&tmk, &tmv, &a};
             GK_CUDA(cudaLaunchKernel(fn, dim3(grid), dim3((kNC + 1) * 32), args, L.total, st),
                     "decode_tma_kernel launch");

@@ -307,3 +307,25 @@ def test_full_config2_sample_parity(cuda_device):
     want = oracle_decode(q.float().cpu().numpy()[sample], kf, vf, bt[sample], ctx[sample],
                          1 / math.sqrt(D), hkv=Hkv, bs=BS)
     np.testing.assert_allclose(out.float().cpu().numpy()[sample], want, atol=2e-2, rtol=0)
+
+
+def test_int8_interleaved_scales_general_path(cuda_device):
+    """Scales stored as one [NB][H][BS][2] array (K at even, V at odd slots): strided,
+    unaligned scale reads take the per-token copy path."""
+    from gollek_b200 import ops
+    ctx = [9, 130, 700]
+    q, k, v, bt, ctx = decode_case(ctx, hq=16, hkv=8, d=128, bs=16, seed=23, kv_std=0.5)
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    both = np.stack([ks, vs], axis=-1)  # [NB, H, BS, 2]
+    scale = 1.0 / math.sqrt(128)
+    qb = O.round_bf16(q)
+    want = oracle_decode(qb, kq, vq, bt, ctx, scale, hkv=8, bs=16, storage=O.INT8, k_scale=ks,
+                         v_scale=vs)
+    bt_d = _t(both, cuda_device).reshape(-1)
+    out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kq, cuda_device),
+                              _t(vq, cuda_device), _t(bt, cuda_device), _t(ctx, cuda_device),
+                              num_kv_heads=8, block_size=16, scale=scale, num_blocks=k.shape[0],
+                              k_scales=bt_d, v_scales=bt_d[1:],
+                              scale_strides=(8 * 16 * 2, 16 * 2, 2))
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
