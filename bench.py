@@ -349,9 +349,9 @@ def bench_decode(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     if args.workload == "longctx":
-        hkv_all = decode_shape("longctx")["hkv"]
-        per = hkv_all // world
-        batch = DecodeBatch("longctx", args.seed, dev, head_lo=rank * per, head_hi=(rank + 1) * per)
+        from gollek_b200.sharding import kv_head_shard
+        lo, hi = kv_head_shard(decode_shape("longctx")["hkv"], world, rank)
+        batch = DecodeBatch("longctx", args.seed, dev, head_lo=lo, head_hi=hi)
     else:
         batch = DecodeBatch(args.workload, args.seed + rank, dev)
     stream = torch.cuda.current_stream(dev)
@@ -517,10 +517,12 @@ def bench_decode(args, world, rank, local):
 def migrate_plan(seed, world):
     """Requests, their prefill (source) rank and block counts; config 4 shapes."""
     import numpy as np
+
+    from gollek_b200.sharding import assign_requests
     rng = np.random.default_rng(seed)
     lens = np.exp(rng.uniform(math.log(2048), math.log(32768), 64)).astype(np.int64)
     nsrc = max(1, world // 2)
-    src_rank = np.arange(64) % nsrc
+    src_rank = np.array(assign_requests(64, world))
     blocks = (lens + 15) // 16
     return lens, src_rank, blocks, nsrc
 
@@ -537,8 +539,8 @@ def bench_migrate(args, world, rank, local):
     bpb = BS * H * D * 2  # bytes per (block, layer), bf16: 32 KiB
     blk = L * bpb         # one block, all layers: 1 MiB, per K and per V
     lens, src_rank, blocks, nsrc = migrate_plan(args.seed, world)
-    is_src = rank < nsrc
-    peer = rank + nsrc if is_src else rank - nsrc
+    from gollek_b200.sharding import migration_peer
+    is_src, peer = migration_peer(world, rank)
     mine = np.where(src_rank == (rank if is_src else peer))[0]
     nblk = int(blocks[mine].sum())
     rng = np.random.default_rng(args.seed + 100 + (rank if is_src else peer))
