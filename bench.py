@@ -566,19 +566,21 @@ def bench_migrate(args, world, rank, local):
     lib = _lib.load()
     hk = (ctypes.c_char * 64)()
     hv = (ctypes.c_char * 64)()
+    ok_, ov_ = ctypes.c_longlong(0), ctypes.c_longlong(0)
     if not is_src:
-        _lib.check(lib.gollek_ipc_get_handle(ctypes.c_void_p(k.data_ptr()), hk))
-        _lib.check(lib.gollek_ipc_get_handle(ctypes.c_void_p(v.data_ptr()), hv))
+        _lib.check(lib.gollek_ipc_get_handle(ctypes.c_void_p(k.data_ptr()), hk, ctypes.byref(ok_)))
+        _lib.check(lib.gollek_ipc_get_handle(ctypes.c_void_p(v.data_ptr()), hv, ctypes.byref(ov_)))
     handles = [None] * world
-    dist.all_gather_object(handles, (bytes(hk), bytes(hv)) if not is_src else None)
+    dist.all_gather_object(handles, (bytes(hk), bytes(hv), ok_.value, ov_.value) if not is_src else None)
     torch.cuda.synchronize()
     dk_ptr = dv_ptr = None
     if is_src:
-        hk_b, hv_b = handles[peer]
+        hk_b, hv_b, off_k, off_v = handles[peer]
         pk, pv = ctypes.c_void_p(), ctypes.c_void_p()
         _lib.check(lib.gollek_ipc_open_handle(hk_b, ctypes.byref(pk)))
         _lib.check(lib.gollek_ipc_open_handle(hv_b, ctypes.byref(pv)))
-        dk_ptr, dv_ptr = pk.value, pv.value
+        base_k, base_v = pk.value, pv.value
+        dk_ptr, dv_ptr = base_k + off_k, base_v + off_v
     s_ids = torch.from_numpy(src_ids).to(dev)
     d_ids = torch.from_numpy(dst_ids).to(dev)
     stream = torch.cuda.current_stream(dev)
@@ -613,8 +615,8 @@ def bench_migrate(args, world, rank, local):
              np.array_equal(gathered[r][1], gathered[r + nsrc][1]) for r in range(nsrc))
     bytes_total = int(blocks.sum()) * blk * 2
     if is_src:
-        lib.gollek_ipc_close_handle(ctypes.c_void_p(dk_ptr))
-        lib.gollek_ipc_close_handle(ctypes.c_void_p(dv_ptr))
+        lib.gollek_ipc_close_handle(ctypes.c_void_p(base_k))
+        lib.gollek_ipc_close_handle(ctypes.c_void_p(base_v))
     barrier(world)
     if rank == 0:
         gbs = bytes_total * args.steps / (t_max / 1e3) / 1e9

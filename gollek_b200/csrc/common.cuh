@@ -132,7 +132,7 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t *r) {
 
 // --------------------------------------------------------------- TMA / async
 
-// 2-D tiled TMA load (no multicast) into shared memory, completing on `bar`.
+// 2-D tiled TMA load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
     asm volatile(
@@ -146,7 +146,7 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 1-D bulk copy (no multicast) global -> shared, completing on `bar`; both addresses
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`; both addresses
 // 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes,
                                           uint64_t *bar) {

@@ -11,7 +11,7 @@
 // One CTA = NC consumer warps + 1 producer warp, one CTA per SM.
 //   Producer: works in lane-parallel waves of up to 32 groups, one stage per lane:
 //   each lane reads its group's block-table entries, waits for its stage to be
-//   free and issues 2-D TMA tile loads (SWIZZLE_128B, no multicast) of the group's K
+//   free and issues 2-D TMA tile loads (SWIZZLE_128B, this CTA only) of the group's K
 //   and V rows, completing on the stage's mbarrier; int8 scales come by 4-byte
 //   cp.async.
 //   Consumer warp w owns a ring of SPW stages and takes groups w, w+NC, ... of the

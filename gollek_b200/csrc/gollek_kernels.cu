@@ -77,6 +77,22 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return g_encode;
 }
 
+PFN_cuMemGetAddressRange_v3020 g_range = nullptr;
+std::once_flag g_range_once;
+
+PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+    std::call_once(g_range_once, [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+        cudaGetLastError();
+    });
+    return g_range;
+}
+
 // ------------------------------------------------------------------ device info
 
 std::mutex g_mu;
@@ -662,13 +678,21 @@ int gollek_enable_peer_access(int device, int peer_device) {
     return GOLLEK_OK;
 }
 
-int gollek_ipc_get_handle(const void *dev_ptr, void *handle_out_64) {
+int gollek_ipc_get_handle(const void *dev_ptr, void *handle_out_64, long long *offset_out) {
     t_last_error.clear();
-    if (!dev_ptr || !handle_out_64) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
+    if (!dev_ptr || !handle_out_64 || !offset_out)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
     cudaIpcMemHandle_t h;
     GK_CUDA(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)), "cudaIpcGetMemHandle");
     static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
     memcpy(handle_out_64, &h, sizeof(h));
+    auto range = address_range_fn();
+    if (!range) return fail(GOLLEK_ERR_UNSUPPORTED, "cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "cuMemGetAddressRange failed");
+    *offset_out = static_cast<long long>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
     return GOLLEK_OK;
 }
 

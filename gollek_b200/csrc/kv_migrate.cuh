@@ -4,7 +4,7 @@
 // Work is cut into 64 KiB segments of (block, K|V) so that a few long requests
 // still spread over every SM.  A thread moves 4 x 16 bytes per step: four
 // independent loads from local HBM in flight, then four 16-byte stores, which go
-// over NVLink when the destination is a peer's memory.  No TMA, no multicast.
+// over NVLink when the destination is a peer's memory.  Plain loads and stores only.
 #pragma once
 
 #include "common.cuh"

@@ -206,9 +206,12 @@ GOLLEK_API int gollek_kv_block_checksum(const void *pool, const int *blocks, int
 /* Enables `device` to access `peer_device`'s memory (idempotent). */
 GOLLEK_API int gollek_enable_peer_access(int device, int peer_device);
 
-/* CUDA IPC for one-process-per-GPU deployments: export a device allocation as a
- * 64-byte handle, map a peer process's handle into this process, unmap it. */
-GOLLEK_API int gollek_ipc_get_handle(const void *dev_ptr, void *handle_out_64);
+/* CUDA IPC for one-process-per-GPU deployments: export the device allocation holding
+ * dev_ptr as a 64-byte handle plus dev_ptr's byte offset inside that allocation (the
+ * importer adds it to the base that gollek_ipc_open_handle returns); map a peer
+ * process's handle into this process; unmap it. */
+GOLLEK_API int gollek_ipc_get_handle(const void *dev_ptr, void *handle_out_64,
+                                     long long *offset_out);
 GOLLEK_API int gollek_ipc_open_handle(const void *handle_64, void **dev_ptr_out);
 GOLLEK_API int gollek_ipc_close_handle(void *dev_ptr);
 
