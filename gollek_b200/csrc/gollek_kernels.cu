@@ -444,6 +444,30 @@ int status_to_code(unsigned v) {
     return GOLLEK_OK;
 }
 
+// ------------------------------------------------------------ no-alloc scratch
+
+// Split-K scratch of gollek_paged_attention_v2_noalloc: a static device array, so that
+// entry point never allocates.  Host code cannot use the array's name as a device
+// address; noalloc_scratch() looks the address up per device (with it current).
+__device__ __align__(256) unsigned char g_noalloc_scratch[GOLLEK_NOALLOC_SCRATCH_BYTES];
+
+std::mutex g_na_mu;
+std::map<int, void *> g_na_ptr;
+
+int noalloc_scratch(int dev, void **out) {
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    auto it = g_na_ptr.find(dev);
+    if (it != g_na_ptr.end()) {
+        *out = it->second;
+        return GOLLEK_OK;
+    }
+    void *p = nullptr;
+    GK_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
+    g_na_ptr[dev] = p;
+    *out = p;
+    return GOLLEK_OK;
+}
+
 }  // namespace
 }  // namespace gk
 
@@ -560,6 +584,67 @@ size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_heads, int 
     if (num_seqs <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0)
         return 0;
     return ws_bytes(num_seqs, num_q_heads, num_kv_heads, head_dim);
+}
+
+int gollek_paged_attention_v2_noalloc(void *out, const void *q, const void *k_cache,
+                                      const void *v_cache, const float *k_scales,
+                                      const float *v_scales, const int *block_tables,
+                                      const int *context_lens, int num_seqs, int num_q_heads,
+                                      int num_kv_heads, int head_dim, int block_size,
+                                      int max_blocks_per_seq, int num_blocks, long long page_stride,
+                                      int q_dtype, int kv_dtype, long long scale_page_stride,
+                                      long long scale_head_stride, long long scale_token_stride,
+                                      float scale, float soft_cap, int sliding_window,
+                                      void *stream) {
+    t_last_error.clear();
+    V2 p{};
+    p.out = out;
+    p.q = q;
+    p.k = k_cache;
+    p.v = v_cache;
+    p.ks = k_scales;
+    p.vs = v_scales;
+    p.bt = block_tables;
+    p.ctx = context_lens;
+    p.S = num_seqs;
+    p.Hq = num_q_heads;
+    p.Hkv = num_kv_heads;
+    p.D = head_dim;
+    p.BS = block_size;
+    p.maxB = max_blocks_per_seq;
+    p.num_blocks = num_blocks;
+    p.page_stride = page_stride;
+    p.q_dtype = q_dtype;
+    p.kv_dtype = kv_dtype;
+    p.sps = scale_page_stride;
+    p.shs = scale_head_stride;
+    p.sts = scale_token_stride;
+    p.scale = scale;
+    p.soft_cap = soft_cap;
+    p.window = sliding_window;
+    p.norm_eps = 1e-9f;
+    p.stream = stream;
+    int rc = check_v2(p);
+    if (rc) return rc;
+    if (p.S == 0) return GOLLEK_OK;
+    const size_t need = ws_bytes(p.S, p.Hq, p.Hkv, p.D);
+    if (need > GOLLEK_NOALLOC_SCRATCH_BYTES)
+        return fail(GOLLEK_ERR_WORKSPACE,
+                    "no-alloc decode needs %zu bytes of split-K scratch; its static buffer holds %u "
+                    "(use gollek_paged_attention_v2 with a workspace)",
+                    need, GOLLEK_NOALLOC_SCRATCH_BYTES);
+    int dev = 0;
+    GK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    void *scratch = nullptr;
+    rc = noalloc_scratch(dev, &scratch);
+    if (rc) return rc;
+    // The arrival counters must start at zero; a previous call leaves them zeroed unless
+    // it gave up half way, so clear them on every call.
+    GK_CUDA(cudaMemsetAsync(scratch, 0, ws_counters_bytes(p.S, p.Hkv), static_cast<cudaStream_t>(stream)),
+            "cudaMemsetAsync(no-alloc scratch counters)");
+    p.workspace = scratch;
+    p.workspace_bytes = GOLLEK_NOALLOC_SCRATCH_BYTES;
+    return run_v2(p);
 }
 
 int gollek_kv_append(const void *key, const void *value, int src_dtype, const int *token_seq,

@@ -140,6 +140,35 @@ GOLLEK_API int gollek_paged_attention_v2(void *out, const void *q, const void *k
 GOLLEK_API size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
                                              int head_dim);
 
+/*
+ * Decode attention that allocates nothing.  No counterpart in the reference: this entry
+ * point exists for callers that cannot allocate device memory themselves -- a caller
+ * running inside a CUDA graph being captured elsewhere, a real-time or embedded host that
+ * forbids allocation after start-up, or an FFM/JNI host whose memory allocator is not
+ * CUDA-aware -- and so can neither call cudaMalloc nor hand the library a workspace.
+ *
+ * Same arguments and results as gollek_paged_attention_v2, without the workspace pair.
+ * The split-K scratch is a static device array of GOLLEK_NOALLOC_SCRATCH_BYTES built into
+ * the library (every GPU that loads the library holds it until the process exits).
+ *   - Calls whose gollek_paged_attention_workspace_size(...) exceeds that size are
+ *     rejected with GOLLEK_ERR_WORKSPACE; nothing is launched.
+ *   - The first call on a device looks up the array's device address (with that device
+ *     current) and caches it; make that first call before any stream capture.
+ *   - Each call clears the scratch's arrival counters on `stream` before the kernel and
+ *     never calls cudaMalloc, cudaFree or any allocating routine.
+ *   - All calls on a device share the one array: calls that overlap on the GPU (on
+ *     different streams, or from different threads) race on it.  Serialise them on one
+ *     stream.
+ */
+#define GOLLEK_NOALLOC_SCRATCH_BYTES (32u << 20)
+GOLLEK_API int gollek_paged_attention_v2_noalloc(
+    void *out, const void *q, const void *k_cache, const void *v_cache, const float *k_scales,
+    const float *v_scales, const int *block_tables, const int *context_lens, int num_seqs,
+    int num_q_heads, int num_kv_heads, int head_dim, int block_size, int max_blocks_per_seq,
+    int num_blocks, long long page_stride, int q_dtype, int kv_dtype, long long scale_page_stride,
+    long long scale_head_stride, long long scale_token_stride, float scale, float soft_cap,
+    int sliding_window, void *stream);
+
 /* ======================================================================== *
  * KV append (the write path)
  * ======================================================================== */
