@@ -165,6 +165,26 @@ __device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a1, ui
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Four signed bytes -> two f16x2 words holding the same integers exactly: byte b
+// becomes the f16 1024 + (b ^ 0x80) (0x64 exponent byte over the biased byte as
+// mantissa), minus 1152.  lo = bytes 0, 1; hi = bytes 2, 3 (lower byte in the low half).
+__device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
+    uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
+    const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    __half2 ha = __hsub2(*reinterpret_cast<__half2 *>(&a), off);
+    __half2 hb = __hsub2(*reinterpret_cast<__half2 *>(&b), off);
+    lo = *reinterpret_cast<uint32_t *>(&ha);
+    hi = *reinterpret_cast<uint32_t *>(&hb);
+}
+
+// 2^e as a float, exact, for e in [-126, 127].
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
+
+// Unbiased exponent of a positive finite float (x in [2^e, 2^(e+1))); normals only.
+__device__ __forceinline__ int exp_of(float x) { return static_cast<int>((__float_as_uint(x) >> 23) & 0xffu) - 127; }
+
 // Byte offset in a swizzled stage tile of byte `b` of row `r`.
 __device__ __forceinline__ uint32_t swz(int r, int b) {
     return static_cast<uint32_t>((b >> 7) * kSlabBytes + r * 128 +
@@ -249,6 +269,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                       const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
     constexpr int KB = KvType<KV>::kBytes;
     constexpr bool QUANT = KvType<KV>::kQuant;
+    constexpr bool I8MMA = std::is_same<KV, int8_t>::value && D == 128;  // int8 on the tensor pipe
     constexpr int ROW_BYTES = D * KB;
     constexpr int NSLAB = ROW_BYTES / 128;
     constexpr int TILE = NSLAB * kSlabBytes;
@@ -847,6 +868,255 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (2 * t + 1 < G) {
                     cw[2 * G + (2 * t + 1) * D + d0] = o[mt][1];
                     cw[2 * G + (2 * t + 1) * D + d0 + 8] = o[mt][3];
+                }
+            }
+        } else if constexpr (I8MMA) {
+            // ======== int8 KV on the tensor pipe.  The bytes become exact f16 integers
+            // in registers (i8x4_to_f16x2) and meet q in f16 MMAs with fp32 accumulation.
+            // The per-token K scale multiplies the fp32 scores.  The V scale enters the
+            // probabilities relative to a power of two 2^ev that the value accumulators
+            // carry (o holds O * 2^-ev), so the f16 probabilities stay in range whatever
+            // the scale; ev moves only when a group's largest scale leaves [2^(ev-2), 2^(ev+3)).
+            // Head-dim order inside the MMAs: quad lane t owns dims [32t, 32t+32); k-step
+            // kk takes dims 32t+4kk+{0,1,2,3} as MMA columns {2t, 2t+1, 2t+8, 2t+9}, so one
+            // K word is one B fragment pair, and q is loaded in the same order.  Value rows
+            // (head_dim) likewise: lane row group g owns dims [16g, 16g+16); m-tile mt row
+            // g is dim 16g+2mt and row g+8 is dim 16g+2mt+1.
+            constexpr int KS = D / 16;
+            static_assert(D == 128, "int8 tensor-pipe path: head_dim 128");
+            const int g = lane >> 2;
+            const int t = lane & 3;
+            const int R = a.block_size < kRows ? a.block_size : kRows;
+            uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
+            float qmul;  // score multiplier: q_scale times the power of two taken out of q
+            {
+                float qf[32];
+                const long long qrow = ((static_cast<long long>(r.s) * Hkv + r.h) * G + g) * D + 32 * t;
+                if (g < G) {
+                    if (a.q_bf16) {
+                        const uint4 *src = reinterpret_cast<const uint4 *>(
+                            reinterpret_cast<const __nv_bfloat16 *>(a.q) + qrow);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint4 w = __ldg(src + i);
+                            qf[8 * i + 0] = bf16_lo(w.x);
+                            qf[8 * i + 1] = bf16_hi(w.x);
+                            qf[8 * i + 2] = bf16_lo(w.y);
+                            qf[8 * i + 3] = bf16_hi(w.y);
+                            qf[8 * i + 4] = bf16_lo(w.z);
+                            qf[8 * i + 5] = bf16_hi(w.z);
+                            qf[8 * i + 6] = bf16_lo(w.w);
+                            qf[8 * i + 7] = bf16_hi(w.w);
+                        }
+                    } else {
+                        const float4 *src = reinterpret_cast<const float4 *>(
+                            reinterpret_cast<const float *>(a.q) + qrow);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 w = __ldg(src + i);
+                            qf[4 * i + 0] = w.x;
+                            qf[4 * i + 1] = w.y;
+                            qf[4 * i + 2] = w.z;
+                            qf[4 * i + 3] = w.w;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) qf[i] = 0.f;
+                }
+                // keep |q| below the f16 maximum: take a power of two out of q and put
+                // it back on the scores
+                float mx = 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(qf[i]));
+                mx = warp_max(mx);
+                const int eq = mx >= 16384.f ? min(exp_of(mx) - 14, 126) : 0;
+                const float down = pow2i(-eq);
+                qmul = a.q_scale * pow2i(eq);
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const float x0 = qf[4 * kk + 2 * hf] * down;
+                        const float x1 = qf[4 * kk + 2 * hf + 1] * down;
+                        qa[kk][hf] = pack2<__half>(x0, x1);
+                        if constexpr (SPLIT) {
+                            const float2 back = unpack2<__half>(qa[kk][hf]);
+                            ql[kk][hf] = pack2<__half>(x0 - back.x, x1 - back.y);
+                        }
+                    }
+            }
+            float m_run = -INFINITY;  // running max of head g (quad-uniform)
+            float l_run = 0.f;        // this lane's share of head g's normaliser
+            int ev = 0;               // o holds O * 2^-ev
+            bool ev_set = false;
+            float o[KS][4];
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+            for (int j = ((warp - gidx) % NC + NC) % NC; j < r.len; j += NC) {
+                if (*cons_abort) continue;
+                const int stage = warp * SPW + my_slot;
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (++my_slot == SPW) {
+                    my_slot = 0;
+                    my_phase ^= 1;
+                }
+                if (!ok) {
+                    *cons_abort = 1;
+                    continue;
+                }
+                const uint32_t kt = smem_u32(sm_stage) + static_cast<uint32_t>(stage) * 2 * TILE;
+                const uint32_t vt = kt + TILE;
+                const int t0 = (sw.g_lo + r.g + j) * kRows;
+                const int v_lo = max(sw.win_start - t0, 0);
+                const int v_hi = min(sw.len - t0, kRows);
+                // ---------------- raw K and V words and the scales to registers, then free
+                // the stage (int8 rows outside the window are finite integers: no clearing)
+                uint4 kr[2][2], vr[4];
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) kr[nt][hf] = lds_u4(kt + swz(g + 8 * nt, 32 * t + 16 * hf));
+#pragma unroll
+                for (int i = 0; i < 4; ++i) vr[i] = lds_u4(vt + swz(2 * t + (i & 1) + 8 * (i >> 1), 16 * g));
+                float ksc[2][2], vsc[2][2];
+                {
+                    const float *sc = sm_scale + stage * 2 * kRows;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int tk = 8 * nt + 2 * t + e;
+                            const int slot = a.scale_mode == 1 ? tk / R : tk;
+                            ksc[nt][e] = sc[slot];
+                            vsc[nt][e] = sc[kRows + slot];
+                        }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_bar[stage]);
+                // ---------------- scores
+                float s[2][4], s2[2][4];
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[nt][e] = s2[nt][e] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    float(*acc)[4] = (kk & 1) ? s2 : s;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        const uint4 &q4 = kr[nt][kk >> 2];
+                        const uint32_t w = (kk & 3) == 0 ? q4.x : (kk & 3) == 1 ? q4.y : (kk & 3) == 2 ? q4.z : q4.w;
+                        uint32_t b0, b1;
+                        i8x4_to_f16x2(w, b0, b1);
+                        mma_16816<__half>(acc[nt], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+                        if constexpr (SPLIT) mma_16816<__half>(acc[nt], ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
+                    }
+                }
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
+                // ---------------- online softmax for head g over tokens 8nt + 2t + e
+                float p[2][2];
+                bool valid[2][2];
+                float mloc = -INFINITY;
+                float vmax = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int tk = 8 * nt + 2 * t + e;
+                        valid[nt][e] = tk >= v_lo && tk < v_hi;
+                        float x2 = s[nt][e] * qmul * ksc[nt][e];
+                        if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
+                        x2 = valid[nt][e] ? x2 : -INFINITY;
+                        p[nt][e] = x2;
+                        mloc = fmaxf(mloc, x2);
+                        if (valid[nt][e]) vmax = fmaxf(vmax, vsc[nt][e]);
+                    }
+                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+                const float mn = fmaxf(m_run, mloc);
+                const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
+                const float mref = (mn == -INFINITY) ? 0.f : mn;
+                m_run = mn;
+                // the V-scale exponent (warp-uniform: every quad sees the same tokens)
+                int ev_new = ev;
+                if (vmax > 0.f && vmax < INFINITY) {
+                    const int e0 = exp_of(vmax);
+                    if (!ev_set || e0 < ev - 2 || e0 > ev + 2) ev_new = max(-100, min(100, e0));
+                }
+                const float vmul = pow2i(-ev_new);
+                float psum = 0.f;
+                float pv[2][2];
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float pe = fast_exp2(p[nt][e] - mref);
+                        psum += pe;
+                        pv[nt][e] = valid[nt][e] ? pe * (vsc[nt][e] * vmul) : 0.f;
+                    }
+                l_run = l_run * alpha + psum;
+                const uint32_t pb0 = pack2<__half>(pv[0][0], pv[0][1]);
+                const uint32_t pb1 = pack2<__half>(pv[1][0], pv[1][1]);
+                const float fac = ev_set ? alpha * pow2i(max(-126, min(127, ev - ev_new))) : alpha;
+                ev = ev_new;
+                ev_set = true;
+                if (__any_sync(0xffffffffu, fac != 1.f)) {
+                    const float al0 = __shfl_sync(0xffffffffu, fac, 8 * t);      // head 2t
+                    const float al1 = __shfl_sync(0xffffffffu, fac, 8 * t + 4);  // head 2t+1
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt) {
+                        o[mt][0] *= al0;
+                        o[mt][1] *= al1;
+                        o[mt][2] *= al0;
+                        o[mt][3] *= al1;
+                    }
+                }
+                // ---------------- values: rows 2t, 2t+1 (a0, a1) and 2t+8, 2t+9 (a2, a3)
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const uint32_t ra = w == 0 ? vr[0].x : w == 1 ? vr[0].y : w == 2 ? vr[0].z : vr[0].w;
+                    const uint32_t rb = w == 0 ? vr[1].x : w == 1 ? vr[1].y : w == 2 ? vr[1].z : vr[1].w;
+                    const uint32_t rc = w == 0 ? vr[2].x : w == 1 ? vr[2].y : w == 2 ? vr[2].z : vr[2].w;
+                    const uint32_t rd = w == 0 ? vr[3].x : w == 1 ? vr[3].y : w == 2 ? vr[3].z : vr[3].w;
+                    uint32_t a0e, a1e, a0o, a1o, a2e, a3e, a2o, a3o;
+                    i8x4_to_f16x2(__byte_perm(ra, rb, 0x5140), a0e, a1e);  // dims 4w, 4w+1
+                    i8x4_to_f16x2(__byte_perm(ra, rb, 0x7362), a0o, a1o);  // dims 4w+2, 4w+3
+                    i8x4_to_f16x2(__byte_perm(rc, rd, 0x5140), a2e, a3e);
+                    i8x4_to_f16x2(__byte_perm(rc, rd, 0x7362), a2o, a3o);
+                    mma_16816<__half>(o[2 * w], a0e, a1e, a2e, a3e, pb0, pb1);
+                    mma_16816<__half>(o[2 * w + 1], a0o, a1o, a2o, a3o, pb0, pb1);
+                }
+            }
+            gidx += r.len;
+
+            // ---------------- this warp's state -> shared memory (O = o * 2^ev)
+            float *cw = sm_comb + warp * G * (D + 2);
+            l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+            l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+            if (t == 0 && g < G) {
+                cw[g] = m_run;
+                cw[G + g] = l_run;
+            }
+            const float om = pow2i(ev);
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                const int d0 = 16 * g + 2 * mt;
+                if (2 * t < G) {
+                    cw[2 * G + (2 * t) * D + d0] = o[mt][0] * om;
+                    cw[2 * G + (2 * t) * D + d0 + 1] = o[mt][2] * om;
+                }
+                if (2 * t + 1 < G) {
+                    cw[2 * G + (2 * t + 1) * D + d0] = o[mt][1] * om;
+                    cw[2 * G + (2 * t + 1) * D + d0 + 1] = o[mt][3] * om;
                 }
             }
         } else {

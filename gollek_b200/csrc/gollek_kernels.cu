@@ -200,7 +200,8 @@ const void *pick_fast(int kv, int D, int G, bool q_f32) {
             return D == 128 ? pick_g<__half, 128, true>(G) : D == 64 ? pick_g<__half, 64, true>(G) : nullptr;
         case GOLLEK_DTYPE_F32:
             return D == 128 ? pick_g<float, 128, false>(G) : D == 64 ? pick_g<float, 64, false>(G) : nullptr;
-        case GOLLEK_DTYPE_I8:
+        case GOLLEK_DTYPE_I8:  // tensor pipe in f16: fp32 q enters as hi + lo
+            if (q_f32) return D == 128 ? pick_g<int8_t, 128, true>(G) : nullptr;
             return D == 128 ? pick_g<int8_t, 128, false>(G) : nullptr;
         default:
             return nullptr;
@@ -262,6 +263,7 @@ const void *fast_eligible(const V2 &p, int G, long long page_stride) {
     if (page_stride % p.D != 0 || (page_stride * eb) % 16 != 0) return nullptr;
     if (p.S > kMaxFastSeqs) return nullptr;
     if (p.kv_dtype == GOLLEK_DTYPE_I8 && (!p.ks || !p.vs)) return nullptr;
+    if (p.kv_dtype == GOLLEK_DTYPE_I8 && !aligned16(p.q)) return nullptr;  // 16-byte q loads
     if (p.q_dtype != GOLLEK_DTYPE_F32 && p.q_dtype != GOLLEK_DTYPE_BF16) return nullptr;
     const long long rows_per_page = page_stride / p.D;
     if (p.num_blocks > 0 && static_cast<long long>(p.num_blocks) * rows_per_page >= (1LL << 31))

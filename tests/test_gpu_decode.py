@@ -329,3 +329,114 @@ def test_int8_interleaved_scales_general_path(cuda_device):
                               k_scales=bt_d, v_scales=bt_d[1:],
                               scale_strides=(8 * 16 * 2, 16 * 2, 2))
     np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+# ------------------------------------------------------------------ int8 on the tensor pipe
+
+def _int8_call(dev, q, kq, vq, bt, ctx, ks, vs, strides, *, bs=16, hkv=8, window=0, soft_cap=0.0,
+               q_dtype=None):
+    from gollek_b200 import ops
+    scale = 1.0 / math.sqrt(q.shape[-1])
+    qd = _t(q, dev) if q_dtype is None else _t(q, dev, q_dtype)
+    return ops.paged_attention(qd, _t(kq, dev), _t(vq, dev), _t(bt, dev), _t(ctx, dev),
+                               num_kv_heads=hkv, block_size=bs, scale=scale, num_blocks=kq.shape[0],
+                               k_scales=_t(ks, dev), v_scales=_t(vs, dev), scale_strides=strides,
+                               sliding_window=window, soft_cap=soft_cap)
+
+
+def test_int8_fp32_query(cuda_device):
+    """fp32 q with int8 KV: q enters the f16 MMAs as hi + lo halves."""
+    ctx = [7, 260, 1500]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=24, kv_std=0.5)
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    want = oracle_decode(q, kq, vq, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16, storage=O.INT8,
+                         k_scale=ks, v_scale=vs)
+    out = _int8_call(cuda_device, q, kq, vq, bt, ctx, ks, vs, (8 * 16, 16, 1))
+    np.testing.assert_allclose(out.cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+def test_int8_large_query_magnitude(cuda_device):
+    """|q| far above the f16 range: a power of two is taken out of q and put back on the
+    scores."""
+    ctx = [50, 300]
+    q, k, v, bt, ctx = decode_case(ctx, hq=16, hkv=8, d=128, bs=16, seed=25, kv_std=0.5)
+    q = O.round_bf16(q * np.float32(3e5))
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    scale = 1.0 / math.sqrt(128)
+    want = oracle_decode(q, kq, vq, bt, ctx, scale, hkv=8, bs=16, storage=O.INT8, k_scale=ks,
+                         v_scale=vs)
+    out = _int8_call(cuda_device, q, kq, vq, bt, ctx, ks, vs, (8 * 16, 16, 1), q_dtype=torch.bfloat16)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+
+
+def test_int8_scales_spanning_decades(cuda_device):
+    """Page scales from 1e-4 to 1e3 in one sequence: the power of two carried by the value
+    accumulators moves with them."""
+    rng = np.random.default_rng(26)
+    ctx = [40, 700, 2100]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=26, kv_std=0.5)
+    f = (10.0 ** rng.uniform(-4, 3, size=(k.shape[0], 1, 1, 1))).astype(np.float32)
+    k = k * np.float32(0.05)  # keep scores moderate; V carries the wide range
+    v = v * f
+    for per_token in (True, False):
+        if per_token:
+            kq, ks = quantize_rows_int8(k)
+            vq, vs = quantize_rows_int8(v)
+            strides, ks_t, vs_t = (8 * 16, 16, 1), ks, vs
+        else:
+            kq, ks = quantize_pages_int8(k)
+            vq, vs = quantize_pages_int8(v)
+            strides = (8, 1, 0)
+            ks_t = np.repeat(ks[:, :, None], 16, axis=2)
+            vs_t = np.repeat(vs[:, :, None], 16, axis=2)
+        qb = O.round_bf16(q)
+        want = oracle_decode(qb, kq, vq, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16, storage=O.INT8,
+                             k_scale=ks_t, v_scale=vs_t)
+        got = _int8_call(cuda_device, qb, kq, vq, bt, ctx, ks, vs, strides,
+                         q_dtype=torch.bfloat16).float().cpu().numpy()
+        # outputs span decades too: 2e-2 absolute, or 1e-2 of the row's own scale
+        err = np.abs(got - want)
+        bound = np.maximum(2e-2 * np.minimum(1.0, np.abs(want).max(axis=-1, keepdims=True)),
+                           1e-2 * np.abs(want).max(axis=-1, keepdims=True))
+        assert (err <= bound).all(), (per_token, float((err / bound).max()))
+
+
+@pytest.mark.parametrize("bs", [8, 32])
+def test_int8_block_sizes(cuda_device, bs):
+    ctx = [3, 77, 640]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=bs, seed=27, kv_std=0.5)
+    qb = O.round_bf16(q)
+    for per_token in (True, False):
+        if per_token:
+            kq, ks = quantize_rows_int8(k)
+            vq, vs = quantize_rows_int8(v)
+            strides, ks_t, vs_t = (8 * bs, bs, 1), ks, vs
+        else:
+            kq, ks = quantize_pages_int8(k)
+            vq, vs = quantize_pages_int8(v)
+            strides = (8, 1, 0)
+            ks_t = np.repeat(ks[:, :, None], bs, axis=2)
+            vs_t = np.repeat(vs[:, :, None], bs, axis=2)
+        want = oracle_decode(qb, kq, vq, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=bs, storage=O.INT8,
+                             k_scale=ks_t, v_scale=vs_t)
+        got = _int8_call(cuda_device, qb, kq, vq, bt, ctx, ks, vs, strides, bs=bs,
+                         q_dtype=torch.bfloat16)
+        np.testing.assert_allclose(got.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("window,soft_cap", [(100, 0.0), (0, 30.0), (40, 5.0)])
+def test_int8_window_and_softcap(cuda_device, window, soft_cap):
+    ctx = [10, 150, 1000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=16, hkv=8, d=128, bs=16, seed=28, kv_std=0.5)
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    qb = O.round_bf16(q)
+    want = oracle_decode(qb, kq, vq, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16, storage=O.INT8,
+                         k_scale=ks, v_scale=vs, window=window, soft_cap=soft_cap)
+    got = _int8_call(cuda_device, qb, kq, vq, bt, ctx, ks, vs, (8 * 16, 16, 1), window=window,
+                     soft_cap=soft_cap, q_dtype=torch.bfloat16)
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, atol=2e-2, rtol=0)
