@@ -35,40 +35,9 @@
 
 #include <type_traits>
 
-#include "common.cuh"
+#include "decode_common.cuh"
 
 namespace gk {
-
-constexpr int kRows = 16;          // tokens per stage
-constexpr int kSlabBytes = kRows * 128;
-constexpr int kMaxSplits = 64;     // split-K pieces per (sequence, kv-head) at most
-constexpr int kMaxFastSeqs = 16384;
-constexpr int kMinRunGroups = 8;   // smallest per-CTA range, in groups
-// Cost of starting a run (a q load, a merge of the warp states, maybe a split-K
-// exchange), in 16-token groups; CTAs are balanced on groups + kRunCost per run.
-constexpr int kRunCost = 16;
-
-struct DecodeArgs {
-    void *out;
-    const void *q;
-    const float *k_scales;
-    const float *v_scales;
-    const int *block_tables;
-    const int *context_lens;
-    float *partials;   // split-K partial states: [(s*Hkv+h)*kMaxSplits + piece][2G + G*D]
-    int *counters;     // [num_seqs * num_kv_heads] arrival counters, zero between calls
-    long long page_rows;  // rows of head_dim elements between consecutive pages
-    long long scale_page_stride, scale_head_stride, scale_token_stride;
-    int num_seqs, num_kv_heads, block_size, max_blocks, num_blocks;
-    int window;           // <= 0: no sliding window
-    int q_bf16;           // 1: q/out bf16, 0: fp32
-    int num_stages;       // NC * stages per warp
-    int scale_mode;       // int8: 0 per-token scales by bulk copy, 1 one scale per page, 2 general
-    float q_scale;        // applied to q when staged: scale*log2(e), or scale with soft-cap
-    float soft_cap;       // > 0: cap*tanh(score/cap)
-    float post_scale;     // log2(e) with soft-cap, else 1
-    float norm_eps;       // 1e-9 (engine path) or 0 (legacy fp32 path)
-};
 
 template <typename KV>
 struct KvType;
@@ -197,19 +166,10 @@ __host__ __device__ constexpr int q_off(int D, int hh, int d) {
     return hh * (D + 4 * (D / 64)) + d + 4 * (d / 64);
 }
 
-__device__ __forceinline__ void store_out(void *out, long long idx, float v, int bf16) {
-    if (bf16)
-        reinterpret_cast<__nv_bfloat16 *>(out)[idx] = __float2bfloat16_rn(v);
-    else
-        reinterpret_cast<float *>(out)[idx] = v;
-}
-
 // Shared-memory carve-up, identical on host and device.
 struct DecodeSmem {
     uint32_t stages, q, p, comb, scales, prefix, cprefix, lens, rstart, misc, bars, total;
 };
-
-__host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 
 __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quant, int D, int G,
                                                          int NC, int stages, int num_seqs,
@@ -244,23 +204,6 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quan
     return L;
 }
 
-// Window of one sequence: groups [g_lo, g_lo + n) of 16 tokens cover [win_start, len).
-struct SeqWin {
-    int len, win_start, g_lo, n;
-};
-
-__device__ __forceinline__ SeqWin seq_win(const DecodeArgs &a, int s) {
-    SeqWin w;
-    int len = a.context_lens[s];
-    const int cap = a.max_blocks * a.block_size;
-    len = len < 0 ? 0 : (len > cap ? cap : len);
-    w.len = len;
-    w.win_start = (a.window > 0 && len > a.window) ? len - a.window : 0;
-    w.g_lo = w.win_start / kRows;
-    w.n = len > 0 ? (len + kRows - 1) / kRows - w.g_lo : 0;
-    return w;
-}
-
 // SPLIT (16-bit KV only): q is wider than the MMA type (fp32 q, or any q with f16 KV)
 // and enters the score MMA as hi + lo halves.
 template <typename KV, int D, int G, int NC, bool SPLIT>
@@ -280,7 +223,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     constexpr int LANE_BYTES = EPL * KB;     // value-pass bytes per lane per row
     constexpr int GP = (G + 3) / 4 * 4;      // p row stride (floats)
     constexpr int QROW = D + 4 * (D / 64);
-    constexpr int NT = (NC + 1) * 32;
     constexpr int CONS = NC * 32;
     static_assert(ROW_BYTES % 128 == 0, "row must be a whole number of 128-byte slabs");
     static_assert(EPL % 2 == 0 && EPC % 4 == 0 && D % 64 == 0, "vector widths");
@@ -332,154 +274,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     }
     __syncthreads();
 
-    // Exclusive prefix of per-sequence group counts (contiguous segment per thread).
-    {
-        const int seg = (S + NT - 1) / NT;
-        const int s0 = min(S, tid * seg);
-        const int s1 = min(S, s0 + seg);
-        int sum = 0, csum = 0, mx = 0;
-        for (int s = s0; s < s1; ++s) {
-            const int raw = a.context_lens[s];
-            if (raw < 0 || raw > a.max_blocks * a.block_size) raise_status(GOLLEK_STATUS_BAD_POSITION);
-            const SeqWin w0 = seq_win(a, s);
-            sm_len[s] = w0.len;
-            const int n = w0.n;
-            sm_prefix[s] = n;
-            sm_cprefix[s] = n > 0 ? n + kRunCost : 0;
-            sum += n;
-            csum += n > 0 ? n + kRunCost : 0;
-            mx = max(mx, n);
-        }
-        int incl = sum, cincl = csum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            const int cv = __shfl_up_sync(0xffffffffu, cincl, o);
-            if (lane >= o) {
-                incl += v;
-                cincl += cv;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        int *warp_tot = reinterpret_cast<int *>(sm_comb);  // scratch before first use
-        int *warp_ctot = warp_tot + 32;
-        if (lane == 31) {
-            warp_tot[warp] = incl;
-            warp_ctot[warp] = cincl;
-        }
-        if (lane == 0) atomicMax(const_cast<int *>(&sm_misc[1]), mx);
-        __syncthreads();
-        if (tid == 0) {
-            int run = 0, crun = 0;
-            for (int w = 0; w <= NC; ++w) {
-                const int t = warp_tot[w], ct = warp_ctot[w];
-                warp_tot[w] = run;
-                warp_ctot[w] = crun;
-                run += t;
-                crun += ct;
-            }
-            sm_prefix[S] = run;
-            sm_cprefix[S] = crun;
-        }
-        __syncthreads();
-        int run = warp_tot[warp] + incl - sum;
-        int crun = warp_ctot[warp] + cincl - csum;
-        for (int s = s0; s < s1; ++s) {
-            const int v = sm_prefix[s], cv = sm_cprefix[s];
-            sm_prefix[s] = run;
-            sm_cprefix[s] = crun;
-            run += v;
-            crun += cv;
-        }
-        __syncthreads();
-    }
-    // Linear group space: unit x = (prefix[s] * Hkv) + h * n_s + g.  CTA ranges are cut
-    // in cost space, where each (sequence, kv-head) costs its groups plus kRunCost, so
-    // a CTA that starts many runs gets fewer groups.  Ranges stay contiguous in x.
-    const long long total = static_cast<long long>(sm_prefix[S]) * Hkv;
-    const long long tcost = static_cast<long long>(sm_cprefix[S]) * Hkv;
-    const int max_n = sm_misc[1];
-    long long per_cost = (tcost + gridDim.x - 1) / gridDim.x;
-    const long long per_floor = (max_n + kMaxSplits - 3) / (kMaxSplits - 2);
-    if (per_cost < per_floor) per_cost = per_floor;
-    if (per_cost < kMinRunGroups) per_cost = kMinRunGroups;
-    const int g_eff = static_cast<int>(min(static_cast<long long>(gridDim.x),
-                                           (tcost + per_cost - 1) / per_cost));
-    // group position where cost c falls (the run's first group for cost inside its
-    // start-up share)
-    auto x_of_cost = [&](long long c) -> long long {
-        if (c >= tcost) return total;
-        int lo = 0, hi = S - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (static_cast<long long>(sm_cprefix[mid]) * Hkv <= c)
-                lo = mid;
-            else
-                hi = mid - 1;
-        }
-        const int n = sm_prefix[lo + 1] - sm_prefix[lo];
-        const int m = n + kRunCost;
-        const int y = static_cast<int>(c - static_cast<long long>(sm_cprefix[lo]) * Hkv);
-        const int h = y / m;
-        const int v = y - h * m;
-        return static_cast<long long>(sm_prefix[lo]) * Hkv + static_cast<long long>(h) * n +
-               (v > kRunCost ? v - kRunCost : 0);
-    };
-    // range starts of all CTAs, computed once
-    for (int b = tid; b <= static_cast<int>(gridDim.x); b += NT)
-        sm_rstart[b] = b >= g_eff ? total : x_of_cost(static_cast<long long>(b) * per_cost);
-    __syncthreads();
-    // the CTA whose range holds group x: the last b with range_start(b) <= x
-    auto owner = [&](long long x) -> int {
-        int lo = 0, hi = g_eff - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (sm_rstart[mid] <= x)
-                lo = mid;
-            else
-                hi = mid - 1;
-        }
-        return lo;
-    };
-    const long long x_beg = sm_rstart[blockIdx.x];
-    const long long x_end = sm_rstart[blockIdx.x + 1];
-
-    // Run containing unit x: sequence s, kv-head h, group offset g within the window,
-    // the run's length and the piece index / piece count of (s, h).
-    struct Run {
-        int s, h, g, len, piece, pieces;
-        long long sh_start, sh_end;
-    };
-    auto run_at = [&](long long x) {
-        Run r;
-        int lo = 0, hi = S - 1;
-        while (lo < hi) {  // last s with prefix[s]*Hkv <= x
-            const int mid = (lo + hi + 1) >> 1;
-            if (static_cast<long long>(sm_prefix[mid]) * Hkv <= x)
-                lo = mid;
-            else
-                hi = mid - 1;
-        }
-        r.s = lo;
-        const int n = sm_prefix[lo + 1] - sm_prefix[lo];  // > 0: x lies inside sequence lo
-        const int y = static_cast<int>(x - static_cast<long long>(sm_prefix[lo]) * Hkv);
-        r.h = y / n;
-        r.g = y - r.h * n;
-        const long long sh_start =
-            static_cast<long long>(sm_prefix[lo]) * Hkv + static_cast<long long>(r.h) * n;
-        const long long sh_end = sh_start + n;
-        r.len = static_cast<int>(min(sh_end, x_end) - x);
-        r.sh_start = sh_start;
-        r.sh_end = sh_end;
-        return r;
-    };
-    // split-K piece index of this CTA's run and the piece count of its (s, h)
-    auto run_pieces = [&](Run &r) {
-        const int first = owner(r.sh_start);
-        r.piece = static_cast<int>(blockIdx.x) - first;
-        r.pieces = owner(r.sh_end - 1) - first + 1;
-    };
+    const Schedule sch = schedule_prologue(a, sm_prefix, sm_cprefix, sm_len, sm_rstart, &sm_misc[1],
+                                           reinterpret_cast<int *>(sm_comb));
+    const long long x_beg = sch.x_beg;
+    const long long x_end = sch.x_end;
+    auto run_at = [&](long long x) { return sch.run_at(x); };
+    auto run_pieces = [&](Run &r) { sch.pieces(r); };
 
     if (warp == NC) {
         // ========================================================= producer
@@ -561,6 +361,11 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     if (!((loaded >> j) & 1)) continue;
                     const long long y = static_cast<long long>(j ? pid1 : pid0) * a.page_rows +
                                         static_cast<long long>(cur.h) * a.block_size + cur.row_off;
+                    if (a.box3d) {  // 16 rows x all slabs in one box each for K and V
+                        tma_load_3d(kdst, &tm_k, 0, static_cast<int>(y), 0, &full_bar[stage]);
+                        tma_load_3d(vdst, &tm_v, 0, static_cast<int>(y), 0, &full_bar[stage]);
+                        continue;
+                    }
 #pragma unroll
                     for (int slab = 0; slab < NSLAB; ++slab) {
                         tma_load_2d(kdst + slab * kSlabBytes + j * R * 128, &tm_k, slab * (128 / KB),

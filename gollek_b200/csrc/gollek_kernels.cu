@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -16,6 +17,7 @@
 
 #include "common.cuh"
 #include "decode_generic.cuh"
+#include "decode_tc.cuh"
 #include "decode_tma.cuh"
 #include "kv_append.cuh"
 #include "kv_migrate.cuh"
@@ -251,24 +253,208 @@ int encode_map(CUtensorMap *m, const void *base, int kv, int D, long long rows, 
     return GOLLEK_OK;
 }
 
-// Eligibility of the TMA kernel; returns its function or nullptr.
-const void *fast_eligible(const V2 &p, int G, long long page_stride) {
+// 4-D map over a bf16 pool with head_dim 128 for the tensor-memory kernel: (64 columns,
+// 8 rows, 2 column slabs, 8-row blocks), strides 256 B / 128 B / 2 KB, so one box of
+// (64, 8, 2, box_rows/8) lands as [row block][slab][8 rows][128 B] in the 128-byte swizzle.
+int encode_map4(CUtensorMap *m, const void *base, long long rows, int box_rows) {
+    auto enc = encode_fn();
+    if (!enc) return fail(GOLLEK_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[4] = {64, 8, 2, static_cast<cuuint64_t>(rows / 8)};
+    cuuint64_t strides[3] = {256, 128, 2048};
+    cuuint32_t box[4] = {64, 8, 2, static_cast<cuuint32_t>(box_rows / 8)};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GOLLEK_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled (4-D) failed (%d)", (int)r);
+    return GOLLEK_OK;
+}
+
+// 3-D map for the mma.sync kernel: (128-byte column slab, row, slab index), strides row
+// pitch / 128 B, box (128 B, 16 rows, all slabs): one box lands as [slab][16 rows][128 B],
+// the kernel's stage layout.
+int encode_map3(CUtensorMap *m, const void *base, int kv, int D, long long rows) {
+    auto enc = encode_fn();
+    if (!enc) return fail(GOLLEK_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    const int eb = dtype_bytes(kv);
+    const int nslab = D * eb / 128;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(128 / eb), static_cast<cuuint64_t>(rows),
+                          static_cast<cuuint64_t>(nslab)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * eb, 128};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / eb), static_cast<cuuint32_t>(kRows),
+                         static_cast<cuuint32_t>(nslab)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, tma_type(kv), 3, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GOLLEK_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+    return GOLLEK_OK;
+}
+
+// Layout conditions shared by the TMA kernels (page tiles, alignment, sizes).
+bool tma_layout_ok(const V2 &p, long long page_stride) {
     const int eb = dtype_bytes(p.kv_dtype);
-    if (eb == 0) return nullptr;
-    const void *fn = pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32);
-    if (!fn) return nullptr;
+    if (eb == 0) return false;
     const bool bs_ok = (p.BS >= 8 && p.BS <= 32 && 32 % p.BS == 0) || (p.BS > 32 && p.BS % 32 == 0);
-    if (!bs_ok) return nullptr;
-    if (!aligned16(p.k) || !aligned16(p.v)) return nullptr;
-    if (page_stride % p.D != 0 || (page_stride * eb) % 16 != 0) return nullptr;
-    if (p.S > kMaxFastSeqs) return nullptr;
-    if (p.kv_dtype == GOLLEK_DTYPE_I8 && (!p.ks || !p.vs)) return nullptr;
-    if (p.kv_dtype == GOLLEK_DTYPE_I8 && !aligned16(p.q)) return nullptr;  // 16-byte q loads
-    if (p.q_dtype != GOLLEK_DTYPE_F32 && p.q_dtype != GOLLEK_DTYPE_BF16) return nullptr;
+    if (!bs_ok) return false;
+    if (!aligned16(p.k) || !aligned16(p.v)) return false;
+    if (page_stride % p.D != 0 || (page_stride * eb) % 16 != 0) return false;
+    if (p.S > kMaxFastSeqs) return false;
+    if (p.kv_dtype == GOLLEK_DTYPE_I8 && (!p.ks || !p.vs)) return false;
+    if (p.kv_dtype == GOLLEK_DTYPE_I8 && !aligned16(p.q)) return false;  // 16-byte q loads
+    if (p.q_dtype != GOLLEK_DTYPE_F32 && p.q_dtype != GOLLEK_DTYPE_BF16) return false;
     const long long rows_per_page = page_stride / p.D;
     if (p.num_blocks > 0 && static_cast<long long>(p.num_blocks) * rows_per_page >= (1LL << 31))
-        return nullptr;
-    return fn;
+        return false;
+    return true;
+}
+
+// Eligibility of the mma.sync TMA kernel; returns its function or nullptr.
+const void *fast_eligible(const V2 &p, int G, long long page_stride) {
+    if (!tma_layout_ok(p, page_stride)) return nullptr;
+    return pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32);
+}
+
+// Split-K scratch: the caller's workspace, or the library's per (device, stream) one.
+int v2_workspace(const V2 &p, int dev, void **ws) {
+    *ws = p.workspace;
+    const size_t need = ws_bytes(p.S, p.Hq, p.Hkv, p.D);
+    if (*ws) {
+        if (p.workspace_bytes < need)
+            return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed", p.workspace_bytes, need);
+        return GOLLEK_OK;
+    }
+    return library_workspace(dev, p.stream, need, ws);
+}
+
+// 2-D tensor maps over the K and V pools: rows of head_dim elements, boxes of 128 bytes
+// x min(block_size, 16) rows.
+int v2_maps(const V2 &p, long long page_stride, CUtensorMap *tmk, CUtensorMap *tmv) {
+    const long long rows_per_page = page_stride / p.D;
+    const long long rows =
+        p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page : (1LL << 31) - 1;
+    const int box_rows = p.BS < kRows ? p.BS : kRows;
+    int rc = encode_map(tmk, p.k, p.kv_dtype, p.D, rows, box_rows);
+    if (!rc) rc = encode_map(tmv, p.v, p.kv_dtype, p.D, rows, box_rows);
+    return rc;
+}
+
+DecodeArgs v2_args(const V2 &p, void *ws, long long page_stride, int stages) {
+    const bool cap = p.soft_cap > 0.f;
+    DecodeArgs a;
+    a.out = p.out;
+    a.q = p.q;
+    a.k_scales = p.ks;
+    a.v_scales = p.vs;
+    a.block_tables = p.bt;
+    a.context_lens = p.ctx;
+    a.counters = static_cast<int *>(ws);
+    a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ws_counters_bytes(p.S, p.Hkv));
+    a.page_rows = page_stride / p.D;
+    a.scale_page_stride = p.sps;
+    a.scale_head_stride = p.shs;
+    a.scale_token_stride = p.sts;
+    a.num_seqs = p.S;
+    a.num_kv_heads = p.Hkv;
+    a.block_size = p.BS;
+    a.max_blocks = p.maxB;
+    a.num_blocks = p.num_blocks;
+    a.window = p.window;
+    a.q_bf16 = p.q_dtype == GOLLEK_DTYPE_BF16;
+    a.num_stages = stages;
+    a.num_vstages = 0;
+    a.box3d = 0;
+    a.scale_mode = 2;
+    if (p.kv_dtype == GOLLEK_DTYPE_I8) {
+        const int R = p.BS < kRows ? p.BS : kRows;
+        if (p.sts == 1 && (p.sps * 4) % 16 == 0 && (p.shs * 4) % 16 == 0 && aligned16(p.ks) &&
+            aligned16(p.vs) && (R * 4) % 16 == 0)
+            a.scale_mode = 0;
+        else if (p.sts == 0)
+            a.scale_mode = 1;
+    }
+    a.q_scale = cap ? p.scale : p.scale * kLog2e;
+    a.soft_cap = p.soft_cap;
+    a.post_scale = cap ? kLog2e : 1.f;
+    a.norm_eps = p.norm_eps;
+    return a;
+}
+
+// Which decode kernel serves bf16 KV: GOLLEK_DECODE_PATH = "auto" (default: the mma.sync
+// kernel, and the tensor-memory kernel for what it alone covers, GQA groups of 16), "tc"
+// (the tensor-memory kernel wherever it applies) or "mma" (never the tensor-memory kernel).
+enum class DecodePath { kAuto, kTc, kMma };
+DecodePath decode_path() {
+    const char *e = std::getenv("GOLLEK_DECODE_PATH");
+    if (e && std::strcmp(e, "tc") == 0) return DecodePath::kTc;
+    if (e && std::strcmp(e, "mma") == 0) return DecodePath::kMma;
+    return DecodePath::kAuto;
+}
+
+template <int G, bool SPLIT>
+const void *tc_kernel() {
+    return reinterpret_cast<const void *>(&decode_tc_kernel<G, SPLIT>);
+}
+
+const void *pick_tc(int G, bool split) {
+    switch (G) {
+        case 1: return split ? tc_kernel<1, true>() : tc_kernel<1, false>();
+        case 2: return split ? tc_kernel<2, true>() : tc_kernel<2, false>();
+        case 4: return split ? tc_kernel<4, true>() : tc_kernel<4, false>();
+        case 8: return split ? tc_kernel<8, true>() : tc_kernel<8, false>();
+        case 16: return split ? tc_kernel<16, true>() : tc_kernel<16, false>();
+        default: return nullptr;
+    }
+}
+
+constexpr int kNotTaken = 1 << 30;
+
+// The tcgen05 kernel (bf16 KV, head_dim 128, GQA group 1-16): launches it, or returns
+// kNotTaken when the case is outside its range.
+int try_tc(const V2 &p, int dev, int G, long long page_stride) {
+    const DecodePath mode = decode_path();
+    if (mode == DecodePath::kMma || p.kv_dtype != GOLLEK_DTYPE_BF16 || p.D != 128) return kNotTaken;
+    if (mode == DecodePath::kAuto && fast_eligible(p, G, page_stride)) return kNotTaken;
+    if (!tma_layout_ok(p, page_stride) || !aligned16(p.q)) return kNotTaken;
+    const bool split = p.q_dtype == GOLLEK_DTYPE_F32;
+    const void *fn = pick_tc(G, split);
+    if (!fn) return kNotTaken;
+    const long long rows_per_page = page_stride / p.D;
+    if (rows_per_page % 8 != 0) return kNotTaken;
+    const int ctas = sm_count(dev);
+    // K / V ring lengths in 32 KB tiles: V tiles are held longer (until the probabilities
+    // exist), so they get the larger ring
+    static const int kRings[][2] = {{2, 4}, {2, 3}, {1, 3}, {2, 2}, {1, 2}};
+    int nk = 0, nv = 0;
+    TcSmem L{};
+    for (const auto &rg : kRings) {
+        L = tc_smem_layout(rg[0], rg[1], split, p.S, ctas);
+        if (L.total <= 227 * 1024) {
+            nk = rg[0];
+            nv = rg[1];
+            break;
+        }
+    }
+    if (!nk) return kNotTaken;
+    void *ws = nullptr;
+    int rc = v2_workspace(p, dev, &ws);
+    if (rc) return rc;
+    const long long rows =
+        p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page : (1LL << 31) - 8;
+    const int box_rows = p.BS < kRows ? p.BS : kRows;
+    CUtensorMap tmk, tmv;
+    rc = encode_map4(&tmk, p.k, rows, box_rows);
+    if (!rc) rc = encode_map4(&tmv, p.v, rows, box_rows);
+    if (rc) return rc;
+    DecodeArgs a = v2_args(p, ws, page_stride, nk);
+    a.num_vstages = nv;
+    GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
+            "cudaFuncSetAttribute");
+    void *args[] = {&tmk, &tmv, &a};
+    GK_CUDA(cudaLaunchKernel(fn, dim3(ctas), dim3(kTcThreads), args, L.total,
+                             static_cast<cudaStream_t>(p.stream)),
+            "decode_tc_kernel launch");
+    return GOLLEK_OK;
 }
 
 int run_v2(const V2 &p) {
@@ -282,6 +468,10 @@ int run_v2(const V2 &p) {
     cudaStream_t st = static_cast<cudaStream_t>(p.stream);
     if (p.S == 0) return GOLLEK_OK;
 
+    {
+        const int rc = try_tc(p, dev, G, page_stride);
+        if (rc != kNotTaken) return rc;
+    }
     const void *fn = fast_eligible(p, G, page_stride);
     if (fn) {
         const int eb = dtype_bytes(p.kv_dtype);
@@ -296,59 +486,22 @@ int run_v2(const V2 &p) {
         DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, kNC, stages, p.S, max_ctas);
         if (L.total > 227 * 1024) fn = nullptr;
         if (fn) {
-            void *ws = p.workspace;
-            const size_t need = ws_bytes(p.S, p.Hq, p.Hkv, p.D);
-            if (ws) {
-                if (p.workspace_bytes < need)
-                    return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed",
-                                p.workspace_bytes, need);
-            } else {
-                int rc = library_workspace(dev, p.stream, need, &ws);
-                if (rc) return rc;
-            }
-            const long long rows_per_page = page_stride / p.D;
-            const long long rows = p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page
-                                                    : (1LL << 31) - 1;
-            const int box_rows = p.BS < kRows ? p.BS : kRows;
-            CUtensorMap tmk, tmv;
-            int rc = encode_map(&tmk, p.k, p.kv_dtype, p.D, rows, box_rows);
-            if (!rc) rc = encode_map(&tmv, p.v, p.kv_dtype, p.D, rows, box_rows);
+            void *ws = nullptr;
+            int rc = v2_workspace(p, dev, &ws);
             if (rc) return rc;
-
-            DecodeArgs a;
-            a.out = p.out;
-            a.q = p.q;
-            a.k_scales = p.ks;
-            a.v_scales = p.vs;
-            a.block_tables = p.bt;
-            a.context_lens = p.ctx;
-            a.counters = static_cast<int *>(ws);
-            a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ws_counters_bytes(p.S, p.Hkv));
-            a.page_rows = rows_per_page;
-            a.scale_page_stride = p.sps;
-            a.scale_head_stride = p.shs;
-            a.scale_token_stride = p.sts;
-            a.num_seqs = p.S;
-            a.num_kv_heads = p.Hkv;
-            a.block_size = p.BS;
-            a.max_blocks = p.maxB;
-            a.num_blocks = p.num_blocks;
-            a.window = p.window;
-            a.q_bf16 = p.q_dtype == GOLLEK_DTYPE_BF16;
-            a.num_stages = stages;
-            a.scale_mode = 2;
-            if (quant) {
-                const int R = p.BS < kRows ? p.BS : kRows;
-                if (p.sts == 1 && (p.sps * 4) % 16 == 0 && (p.shs * 4) % 16 == 0 && aligned16(p.ks) &&
-                    aligned16(p.vs) && (R * 4) % 16 == 0)
-                    a.scale_mode = 0;
-                else if (p.sts == 0)
-                    a.scale_mode = 1;
+            CUtensorMap tmk, tmv;
+            const bool box3d = p.BS >= kRows && p.D * eb >= 256;
+            if (box3d) {
+                const long long rows = p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * (page_stride / p.D)
+                                                        : (1LL << 31) - 1;
+                rc = encode_map3(&tmk, p.k, p.kv_dtype, p.D, rows);
+                if (!rc) rc = encode_map3(&tmv, p.v, p.kv_dtype, p.D, rows);
+            } else {
+                rc = v2_maps(p, page_stride, &tmk, &tmv);
             }
-            a.q_scale = cap ? p.scale : p.scale * log2e;
-            a.soft_cap = p.soft_cap;
-            a.post_scale = cap ? log2e : 1.f;
-            a.norm_eps = p.norm_eps;
+            if (rc) return rc;
+            DecodeArgs a = v2_args(p, ws, page_stride, stages);
+            a.box3d = box3d ? 1 : 0;
 
             GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
                     "cudaFuncSetAttribute");

@@ -440,3 +440,74 @@ def test_int8_window_and_softcap(cuda_device, window, soft_cap):
     got = _int8_call(cuda_device, qb, kq, vq, bt, ctx, ks, vs, (8 * 16, 16, 1), window=window,
                      soft_cap=soft_cap, q_dtype=torch.bfloat16)
     np.testing.assert_allclose(got.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+# ------------------------------------------------------------------ both 16-bit kernels
+
+_PATH_CASES = [
+    # hq, hkv, bs, q_f32, window, soft_cap
+    (32, 8, 16, False, 0, 0.0),
+    (64, 8, 16, True, 0, 0.0),
+    (128, 8, 16, False, 0, 0.0),
+    (8, 8, 16, False, 0, 0.0),
+    (16, 8, 16, True, 0, 0.0),
+    (32, 8, 8, False, 0, 0.0),
+    (32, 8, 32, False, 0, 0.0),
+    (32, 8, 16, False, 100, 0.0),
+    (32, 8, 16, False, 0, 30.0),
+]
+
+
+@pytest.mark.parametrize("path", ["tc", "mma"])
+@pytest.mark.parametrize("hq,hkv,bs,q_f32,window,soft_cap", _PATH_CASES)
+def test_bf16_kernel_paths(cuda_device, monkeypatch, path, hq, hkv, bs, q_f32, window, soft_cap):
+    """bf16 KV through the tcgen05 kernel and through the mma.sync kernel (selected with
+    GOLLEK_DECODE_PATH): contexts that split across CTAs, tiles with 1..8 groups, GQA
+    groups 1-16, fp32 q (hi + lo), block sizes 8/16/32, window and soft-cap."""
+    from gollek_b200 import ops
+    if path == "mma" and hq // hkv > 8:
+        pytest.skip("the mma.sync kernel serves GQA groups up to 8")
+    monkeypatch.setenv("GOLLEK_DECODE_PATH", path)
+    ctx = [9000, 5000, 1, 16, 17, 128, 129, 250, 0, 3000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=128, bs=bs, seed=hq + bs + window, kv_std=0.5)
+    kb, vb = O.round_bf16(k), O.round_bf16(v)
+    qq = q if q_f32 else O.round_bf16(q)
+    scale = 1.0 / math.sqrt(128)
+    want = oracle_decode(qq, kb, vb, bt, ctx, scale, hkv=hkv, bs=bs, window=window, soft_cap=soft_cap)
+    for _ in range(2):  # the split-K scratch must be left zeroed by the first call
+        out = ops.paged_attention(_t(qq, cuda_device) if q_f32 else _t(qq, cuda_device, torch.bfloat16),
+                                  _t(kb, cuda_device, torch.bfloat16), _t(vb, cuda_device, torch.bfloat16),
+                                  _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=hkv,
+                                  block_size=bs, scale=scale, num_blocks=k.shape[0],
+                                  sliding_window=window, soft_cap=soft_cap)
+        got = out.float().cpu().numpy()
+        np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+        assert not got[8].any()
+    assert ops.device_status(cuda_device.index or 0) == 0
+
+
+@pytest.mark.parametrize("path", ["tc", "mma"])
+def test_bf16_nan_outside_the_context(cuda_device, monkeypatch, path):
+    """Pool rows past a sequence's length and before its window hold NaN: they must not
+    reach the output (a zero probability does not cancel a NaN on the tensor pipe)."""
+    from gollek_b200 import ops
+    monkeypatch.setenv("GOLLEK_DECODE_PATH", path)
+    ctx = [37, 300, 1000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=41, kv_std=0.5)
+    kb, vb = O.round_bf16(k), O.round_bf16(v)
+    qb = O.round_bf16(q)
+    window = 200
+    want = oracle_decode(qb, kb, vb, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16, window=window)
+    kn, vn = kb.copy(), vb.copy()
+    for s, c in enumerate(ctx):
+        ws = max(0, int(c) - window)
+        for t in list(range(ws)) + list(range(int(c), ((int(c) + 15) // 16) * 16)):
+            kn[bt[s, t // 16], :, t % 16, :] = np.nan
+            vn[bt[s, t // 16], :, t % 16, :] = np.nan
+    out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kn, cuda_device, torch.bfloat16),
+                              _t(vn, cuda_device, torch.bfloat16), _t(bt, cuda_device),
+                              _t(ctx, cuda_device), num_kv_heads=8, block_size=16,
+                              scale=1 / math.sqrt(128), num_blocks=k.shape[0], sliding_window=window)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
