@@ -23,6 +23,8 @@ __device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status
 // GOLLEK_STATUS_TIMEOUT.  Each try_wait blocks for a hardware-defined slice, so
 // this bounds a wait at well over a second: far beyond any real TMA latency.
 constexpr unsigned kWaitLimit = 1u << 24;
+// Polling rounds (each with a short sleep) before a poll loop gives up.
+constexpr unsigned kPollLimit = 1u << 24;
 
 // ----------------------------------------------------------------- elements
 
@@ -78,6 +80,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         if (mbar_try_wait(bar, parity)) return true;
     raise_status(GOLLEK_STATUS_TIMEOUT);
     return false;
+}
+
+// Non-blocking test of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
 }
 
 // Shared-memory loads/stores by 32-bit shared address.  volatile keeps them ordered

@@ -134,18 +134,15 @@ __device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a1, ui
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Four signed bytes -> two f16x2 words holding the same integers exactly: byte b
+// Four signed bytes -> two f16x2 words holding the integers 1152 + b exactly: byte b
 // becomes the f16 1024 + (b ^ 0x80) (0x64 exponent byte over the biased byte as
-// mantissa), minus 1152.  lo = bytes 0, 1; hi = bytes 2, 3 (lower byte in the low half).
-__device__ __forceinline__ void i8x4_to_f16x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+// mantissa).  lo = bytes 0, 1; hi = bytes 2, 3 (lower byte in the low half).  A dot
+// product over these carries 1152 times the sum of the other operand, which the caller
+// removes once in fp32.
+__device__ __forceinline__ void i8x4_to_f16x2_biased(uint32_t w, uint32_t &lo, uint32_t &hi) {
     const uint32_t u = w ^ 0x80808080u;
-    uint32_t a = __byte_perm(u, 0x64646464u, 0x4140);
-    uint32_t b = __byte_perm(u, 0x64646464u, 0x4342);
-    const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
-    __half2 ha = __hsub2(*reinterpret_cast<__half2 *>(&a), off);
-    __half2 hb = __hsub2(*reinterpret_cast<__half2 *>(&b), off);
-    lo = *reinterpret_cast<uint32_t *>(&ha);
-    hi = *reinterpret_cast<uint32_t *>(&hb);
+    lo = __byte_perm(u, 0x64646464u, 0x4140);
+    hi = __byte_perm(u, 0x64646464u, 0x4342);
 }
 
 // 2^e as a float, exact, for e in [-126, 127].
@@ -260,7 +257,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     // ------------------------------------------------------------ prologue
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
-            mbar_init(&full_bar[i], (QUANT && a.scale_mode != 0) ? 2 : 1);
+            mbar_init(&full_bar[i], (QUANT && a.scale_mode == 2) ? 2 : 1);
             mbar_init(&empty_bar[i], 1);
         }
         fence_barrier_init();
@@ -294,6 +291,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         struct GroupLoc {
             int h, t0, row_off, pid0, pid1, stage, round, len, win_start;
             unsigned loaded;
+            float ks[2], vs[2];  // per-page int8 scales of the group's pages
         };
         auto locate_group = [&](long long x, int gi) {
             GroupLoc q;
@@ -331,93 +329,136 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             }
             return e;
         };
+        // Per-page int8 scales go through registers: loaded one wave ahead of their
+        // wave's issue and stored to the stage's scale slots before the barrier is armed.
+        const bool page_scales = QUANT && a.scale_mode == 1;
+        auto load_scales = [&](GroupLoc &q, bool act) {
+            if constexpr (QUANT) {
+                if (!page_scales || !act) return;
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    if (j >= npg || !((q.loaded >> j) & 1)) continue;
+                    const long long so =
+                        static_cast<long long>(checked(j ? q.pid1 : q.pid0)) * a.scale_page_stride +
+                        static_cast<long long>(q.h) * a.scale_head_stride;
+                    q.ks[j] = __ldg(a.k_scales + so);
+                    q.vs[j] = __ldg(a.v_scales + so);
+                }
+            }
+        };
+        // one group's copies into its stage (the stage is free)
+        auto issue = [&](const GroupLoc &q) {
+            const int stage = q.stage;
+            const int pid0 = checked(q.pid0), pid1 = checked(q.pid1);
+            const unsigned loaded = q.loaded;
+            uint8_t *kdst = sm_stage + static_cast<uint32_t>(stage) * 2 * TILE;
+            uint8_t *vdst = kdst + TILE;
+            if constexpr (QUANT) {
+                if (page_scales) {
+                    float *ks = sm_scale + stage * 2 * kRows;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        if (j >= npg || !((loaded >> j) & 1)) continue;
+                        ks[j] = q.ks[j];
+                        ks[kRows + j] = q.vs[j];
+                    }
+                }
+            }
+            const uint32_t scale_tx = (QUANT && a.scale_mode == 0) ? 2u * R * 4u : 0u;
+            mbar_arrive_expect_tx(&full_bar[stage], static_cast<uint32_t>(__popc(loaded)) *
+                                                        (2u * NSLAB * R * 128u + scale_tx));
+            for (int j = 0; j < npg; ++j) {
+                if (!((loaded >> j) & 1)) continue;
+                const long long y = static_cast<long long>(j ? pid1 : pid0) * a.page_rows +
+                                    static_cast<long long>(q.h) * a.block_size + q.row_off;
+                if (a.box3d) {  // 16 rows x all slabs in one box each for K and V
+                    tma_load_3d(kdst, &tm_k, 0, static_cast<int>(y), 0, &full_bar[stage]);
+                    tma_load_3d(vdst, &tm_v, 0, static_cast<int>(y), 0, &full_bar[stage]);
+                    continue;
+                }
+#pragma unroll
+                for (int slab = 0; slab < NSLAB; ++slab) {
+                    tma_load_2d(kdst + slab * kSlabBytes + j * R * 128, &tm_k, slab * (128 / KB),
+                                static_cast<int>(y), &full_bar[stage]);
+                    tma_load_2d(vdst + slab * kSlabBytes + j * R * 128, &tm_v, slab * (128 / KB),
+                                static_cast<int>(y), &full_bar[stage]);
+                }
+            }
+            if constexpr (QUANT) {
+                float *ks = sm_scale + stage * 2 * kRows;
+                if (a.scale_mode == 0) {
+                    // per-token scales: R contiguous floats per page, one bulk copy each
+                    for (int j = 0; j < npg; ++j) {
+                        if (!((loaded >> j) & 1)) continue;
+                        const long long so = static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
+                                             static_cast<long long>(q.h) * a.scale_head_stride + q.row_off;
+                        bulk_load(ks + j * R, a.k_scales + so, R * 4u, &full_bar[stage]);
+                        bulk_load(ks + kRows + j * R, a.v_scales + so, R * 4u, &full_bar[stage]);
+                    }
+                } else if (a.scale_mode == 2) {
+                    for (int tk = 0; tk < kRows; ++tk) {
+                        const int t = q.t0 + tk;
+                        const int j = tk / R;
+                        if (t >= q.win_start && t < q.len && ((loaded >> j) & 1)) {
+                            const long long so = static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
+                                                 static_cast<long long>(q.h) * a.scale_head_stride +
+                                                 static_cast<long long>(t % a.block_size) * a.scale_token_stride;
+                            cp_async_4(ks + tk, a.k_scales + so);
+                            cp_async_4(ks + kRows + tk, a.v_scales + so);
+                        }
+                    }
+                    cp_async_mbar_arrive_noinc(&full_bar[stage]);
+                }
+            }
+        };
         int gbase = 0;
         bool aborted = false;
         long long xw = x_beg;
         int nw = static_cast<int>(min(static_cast<long long>(W), x_end - xw));
-        GroupLoc cur{};
+        // cur: this wave (ids and scales ready); nxt: next wave (ids ready, scales in
+        // flight); the wave after that is looked up at the top of each round.
+        GroupLoc cur{}, nxt{};
         if (lane < nw) cur = locate_group(xw + lane, gbase + lane);
+        load_scales(cur, lane < nw);
+        long long xn = xw + nw;
+        int gn = gbase + nw;
+        int nw_next = static_cast<int>(min(static_cast<long long>(W), x_end - xn));
+        if (lane < nw_next) nxt = locate_group(xn + lane, gn + lane);
         while (xw < x_end) {
-            // look up the next wave while this one waits and issues
-            const long long xn = xw + nw;
-            const int gn = gbase + nw;
-            const int nw_next = static_cast<int>(min(static_cast<long long>(W), x_end - xn));
-            GroupLoc nxt{};
-            if (lane < nw_next) nxt = locate_group(xn + lane, gn + lane);
+            const long long xnn = xn + nw_next;
+            const int gnn = gn + nw_next;
+            const int nw_nn = static_cast<int>(min(static_cast<long long>(W), x_end - xnn));
+            GroupLoc nn{};
+            if (lane < nw_nn) nn = locate_group(xnn + lane, gnn + lane);
+            load_scales(nxt, lane < nw_next);
 
-            const bool act = lane < nw;
+            // Issue this wave: every lane polls its own stage (non-blocking, so lanes whose
+            // stage is free issue at once) until all have issued.
+            bool pending = lane < nw;
             bool ok = true;
-            if (act && cur.round > 0) ok = mbar_wait(&empty_bar[cur.stage], (cur.round - 1) & 1);
-            if (act && ok) {
-                const int stage = cur.stage;
-                const int pid0 = checked(cur.pid0), pid1 = checked(cur.pid1);
-                const unsigned loaded = cur.loaded;
-                uint8_t *kdst = sm_stage + static_cast<uint32_t>(stage) * 2 * TILE;
-                uint8_t *vdst = kdst + TILE;
-                const uint32_t scale_tx = (QUANT && a.scale_mode == 0) ? 2u * R * 4u : 0u;
-                mbar_arrive_expect_tx(&full_bar[stage], static_cast<uint32_t>(__popc(loaded)) *
-                                                            (2u * NSLAB * R * 128u + scale_tx));
-                for (int j = 0; j < npg; ++j) {
-                    if (!((loaded >> j) & 1)) continue;
-                    const long long y = static_cast<long long>(j ? pid1 : pid0) * a.page_rows +
-                                        static_cast<long long>(cur.h) * a.block_size + cur.row_off;
-                    if (a.box3d) {  // 16 rows x all slabs in one box each for K and V
-                        tma_load_3d(kdst, &tm_k, 0, static_cast<int>(y), 0, &full_bar[stage]);
-                        tma_load_3d(vdst, &tm_v, 0, static_cast<int>(y), 0, &full_bar[stage]);
-                        continue;
-                    }
-#pragma unroll
-                    for (int slab = 0; slab < NSLAB; ++slab) {
-                        tma_load_2d(kdst + slab * kSlabBytes + j * R * 128, &tm_k, slab * (128 / KB),
-                                    static_cast<int>(y), &full_bar[stage]);
-                        tma_load_2d(vdst + slab * kSlabBytes + j * R * 128, &tm_v, slab * (128 / KB),
-                                    static_cast<int>(y), &full_bar[stage]);
-                    }
+            for (unsigned spins = 0;; ++spins) {
+                if (pending && (cur.round == 0 || mbar_test(&empty_bar[cur.stage], (cur.round - 1) & 1))) {
+                    issue(cur);
+                    pending = false;
                 }
-                if constexpr (QUANT) {
-                    float *ks = sm_scale + stage * 2 * kRows;
-                    if (a.scale_mode == 0) {
-                        // per-token scales: R contiguous floats per page, one bulk copy each
-                        for (int j = 0; j < npg; ++j) {
-                            if (!((loaded >> j) & 1)) continue;
-                            const long long so =
-                                static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
-                                static_cast<long long>(cur.h) * a.scale_head_stride + cur.row_off;
-                            bulk_load(ks + j * R, a.k_scales + so, R * 4u, &full_bar[stage]);
-                            bulk_load(ks + kRows + j * R, a.v_scales + so, R * 4u, &full_bar[stage]);
-                        }
-                    } else if (a.scale_mode == 1) {
-                        // one scale per (page, kv-head): slot j of the stage
-                        for (int j = 0; j < npg; ++j) {
-                            if (!((loaded >> j) & 1)) continue;
-                            const long long so =
-                                static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
-                                static_cast<long long>(cur.h) * a.scale_head_stride;
-                            cp_async_4(ks + j, a.k_scales + so);
-                            cp_async_4(ks + kRows + j, a.v_scales + so);
-                        }
-                        cp_async_mbar_arrive_noinc(&full_bar[stage]);
-                    } else {
-                        for (int tk = 0; tk < kRows; ++tk) {
-                            const int t = cur.t0 + tk;
-                            const int j = tk / R;
-                            if (t >= cur.win_start && t < cur.len && ((loaded >> j) & 1)) {
-                                const long long so =
-                                    static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
-                                    static_cast<long long>(cur.h) * a.scale_head_stride +
-                                    static_cast<long long>(t % a.block_size) * a.scale_token_stride;
-                                cp_async_4(ks + tk, a.k_scales + so);
-                                cp_async_4(ks + kRows + tk, a.v_scales + so);
-                            }
-                        }
-                        cp_async_mbar_arrive_noinc(&full_bar[stage]);
+                if (!__any_sync(0xffffffffu, pending)) break;
+                if (spins > kPollLimit) {
+                    if (pending) {
+                        raise_status(GOLLEK_STATUS_TIMEOUT);
+                        ok = false;
                     }
+                    break;
                 }
+                __nanosleep(20);
             }
             xw = xn;
             gbase = gn;
             nw = nw_next;
             cur = nxt;
+            xn = xnn;
+            gn = gnn;
+            nw_next = nw_nn;
+            nxt = nn;
             if (!__all_sync(0xffffffffu, ok)) {
                 aborted = true;
                 break;
@@ -677,7 +718,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             }
         } else if constexpr (I8MMA) {
             // ======== int8 KV on the tensor pipe.  The bytes become exact f16 integers
-            // in registers (i8x4_to_f16x2) and meet q in f16 MMAs with fp32 accumulation.
+            // 1152 + b in registers (i8x4_to_f16x2_biased) and meet q in f16 MMAs with fp32
+            // accumulation; the bias is removed once in fp32 (1152 * sum(q) from each score,
+            // 1152 * the probability mass from each value accumulator).
             // The per-token K scale multiplies the fp32 scores.  The V scale enters the
             // probabilities relative to a power of two 2^ev that the value accumulators
             // carry (o holds O * 2^-ev), so the f16 probabilities stay in range whatever
@@ -693,7 +736,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             const int t = lane & 3;
             const int R = a.block_size < kRows ? a.block_size : kRows;
             uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
-            float qmul;  // score multiplier: q_scale times the power of two taken out of q
+            float qmul;         // score multiplier: q_scale times the power of two taken out of q
+            float qsum = 0.f;   // head g's sum of the f16 q values the MMAs see
             {
                 float qf[32];
                 const long long qrow = ((static_cast<long long>(r.s) * Hkv + r.h) * G + g) * D + 32 * t;
@@ -745,14 +789,21 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         const float x0 = qf[4 * kk + 2 * hf] * down;
                         const float x1 = qf[4 * kk + 2 * hf + 1] * down;
                         qa[kk][hf] = pack2<__half>(x0, x1);
+                        const float2 back = unpack2<__half>(qa[kk][hf]);
+                        qsum += back.x + back.y;
                         if constexpr (SPLIT) {
-                            const float2 back = unpack2<__half>(qa[kk][hf]);
                             ql[kk][hf] = pack2<__half>(x0 - back.x, x1 - back.y);
+                            const float2 lo2 = unpack2<__half>(ql[kk][hf]);
+                            qsum += lo2.x + lo2.y;
                         }
                     }
+                qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+                qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
             }
+            const float qbias = 1152.f * qsum;  // the biased K bytes add this to head g's scores
             float m_run = -INFINITY;  // running max of head g (quad-uniform)
             float l_run = 0.f;        // this lane's share of head g's normaliser
+            float ps_run = 0.f;       // this lane's share of head g's probability mass in o
             int ev = 0;               // o holds O * 2^-ev
             bool ev_set = false;
             float o[KS][4];
@@ -789,16 +840,29 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 for (int i = 0; i < 4; ++i) vr[i] = lds_u4(vt + swz(2 * t + (i & 1) + 8 * (i >> 1), 16 * g));
                 float ksc[2][2], vsc[2][2];
                 {
-                    const float *sc = sm_scale + stage * 2 * kRows;
+                    const uint32_t sc = smem_u32(sm_scale) + static_cast<uint32_t>(stage) * 2 * kRows * 4;
+                    if (a.scale_mode == 1) {  // one scale per page (slot = token / R)
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int tk = 8 * nt + 2 * t + e;
-                            const int slot = a.scale_mode == 1 ? tk / R : tk;
-                            ksc[nt][e] = sc[slot];
-                            vsc[nt][e] = sc[kRows + slot];
+                        for (int nt = 0; nt < 2; ++nt) {
+                            const int slot = (8 * nt) / R;
+                            const uint32_t k1 = sc + static_cast<uint32_t>(slot) * 4;
+                            float kf, vf;
+                            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(kf) : "r"(k1));
+                            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(vf) : "r"(k1 + kRows * 4));
+                            ksc[nt][0] = ksc[nt][1] = kf;
+                            vsc[nt][0] = vsc[nt][1] = vf;
                         }
+                    } else {  // per token: tokens 2t, 2t+1 of each n-tile are adjacent
+#pragma unroll
+                        for (int nt = 0; nt < 2; ++nt) {
+                            const uint2 kw = lds_u2(sc + (8 * nt + 2 * t) * 4);
+                            const uint2 vw = lds_u2(sc + (kRows + 8 * nt + 2 * t) * 4);
+                            ksc[nt][0] = __uint_as_float(kw.x);
+                            ksc[nt][1] = __uint_as_float(kw.y);
+                            vsc[nt][0] = __uint_as_float(vw.x);
+                            vsc[nt][1] = __uint_as_float(vw.y);
+                        }
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty_bar[stage]);
@@ -816,7 +880,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         const uint4 &q4 = kr[nt][kk >> 2];
                         const uint32_t w = (kk & 3) == 0 ? q4.x : (kk & 3) == 1 ? q4.y : (kk & 3) == 2 ? q4.z : q4.w;
                         uint32_t b0, b1;
-                        i8x4_to_f16x2(w, b0, b1);
+                        i8x4_to_f16x2_biased(w, b0, b1);
                         mma_16816<__half>(acc[nt], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
                         if constexpr (SPLIT) mma_16816<__half>(acc[nt], ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
                     }
@@ -824,7 +888,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
+                    for (int e = 0; e < 2; ++e) s[nt][e] = (s[nt][e] + s2[nt][e]) - qbias;
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
                 float p[2][2];
                 bool valid[2][2];
@@ -871,7 +935,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 l_run = l_run * alpha + psum;
                 const uint32_t pb0 = pack2<__half>(pv[0][0], pv[0][1]);
                 const uint32_t pb1 = pack2<__half>(pv[1][0], pv[1][1]);
+                const float2 pr0 = unpack2<__half>(pb0), pr1 = unpack2<__half>(pb1);
                 const float fac = ev_set ? alpha * pow2i(max(-126, min(127, ev - ev_new))) : alpha;
+                ps_run = ps_run * fac + ((pr0.x + pr0.y) + (pr1.x + pr1.y));
                 ev = ev_new;
                 ev_set = true;
                 if (__any_sync(0xffffffffu, fac != 1.f)) {
@@ -893,10 +959,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     const uint32_t rc = w == 0 ? vr[2].x : w == 1 ? vr[2].y : w == 2 ? vr[2].z : vr[2].w;
                     const uint32_t rd = w == 0 ? vr[3].x : w == 1 ? vr[3].y : w == 2 ? vr[3].z : vr[3].w;
                     uint32_t a0e, a1e, a0o, a1o, a2e, a3e, a2o, a3o;
-                    i8x4_to_f16x2(__byte_perm(ra, rb, 0x5140), a0e, a1e);  // dims 4w, 4w+1
-                    i8x4_to_f16x2(__byte_perm(ra, rb, 0x7362), a0o, a1o);  // dims 4w+2, 4w+3
-                    i8x4_to_f16x2(__byte_perm(rc, rd, 0x5140), a2e, a3e);
-                    i8x4_to_f16x2(__byte_perm(rc, rd, 0x7362), a2o, a3o);
+                    i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x5140), a0e, a1e);  // dims 4w, 4w+1
+                    i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x7362), a0o, a1o);  // dims 4w+2, 4w+3
+                    i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x5140), a2e, a3e);
+                    i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x7362), a2o, a3o);
                     mma_16816<__half>(o[2 * w], a0e, a1e, a2e, a3e, pb0, pb1);
                     mma_16816<__half>(o[2 * w + 1], a0o, a1o, a2o, a3o, pb0, pb1);
                 }
@@ -911,17 +977,22 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 cw[g] = m_run;
                 cw[G + g] = l_run;
             }
+            // the biased V bytes added 1152 times each head's probability mass to o
+            ps_run += __shfl_xor_sync(0xffffffffu, ps_run, 1);
+            ps_run += __shfl_xor_sync(0xffffffffu, ps_run, 2);
+            const float bias0 = 1152.f * __shfl_sync(0xffffffffu, ps_run, 8 * t);      // head 2t
+            const float bias1 = 1152.f * __shfl_sync(0xffffffffu, ps_run, 8 * t + 4);  // head 2t+1
             const float om = pow2i(ev);
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
                 const int d0 = 16 * g + 2 * mt;
                 if (2 * t < G) {
-                    cw[2 * G + (2 * t) * D + d0] = o[mt][0] * om;
-                    cw[2 * G + (2 * t) * D + d0 + 1] = o[mt][2] * om;
+                    cw[2 * G + (2 * t) * D + d0] = (o[mt][0] - bias0) * om;
+                    cw[2 * G + (2 * t) * D + d0 + 1] = (o[mt][2] - bias0) * om;
                 }
                 if (2 * t + 1 < G) {
-                    cw[2 * G + (2 * t + 1) * D + d0] = o[mt][1] * om;
-                    cw[2 * G + (2 * t + 1) * D + d0 + 1] = o[mt][3] * om;
+                    cw[2 * G + (2 * t + 1) * D + d0] = (o[mt][1] - bias1) * om;
+                    cw[2 * G + (2 * t + 1) * D + d0 + 1] = (o[mt][3] - bias1) * om;
                 }
             }
         } else {

@@ -162,7 +162,21 @@ size_t ws_bytes(int S, int Hq, int Hkv, int D) {
 
 // ------------------------------------------------------------------ fast path
 
-constexpr int kNC = 8;                  // consumer warps per CTA (one CTA per SM)
+// Consumer warps per CTA (one CTA per SM), by KV type: the int8 and fp32 consumers are
+// latency-bound per group and gain from more warps; 16-bit KV keeps the registers for
+// its staged fragments.
+#ifndef GK_NC_I8
+#define GK_NC_I8 8
+#endif
+#ifndef GK_NC_F32
+#define GK_NC_F32 12
+#endif
+constexpr int kNC = 8;
+template <typename KV>
+constexpr int nc_of() {
+    return std::is_same<KV, int8_t>::value ? GK_NC_I8 : std::is_same<KV, float>::value ? GK_NC_F32 : kNC;
+}
+int nc_for(int kv) { return kv == GOLLEK_DTYPE_I8 ? GK_NC_I8 : kv == GOLLEK_DTYPE_F32 ? GK_NC_F32 : kNC; }
 constexpr uint32_t kSmemBudget = 224 * 1024;
 constexpr int kMaxStagesPerWarp = 6;
 
@@ -174,7 +188,7 @@ struct Launch {
 
 template <typename KV, int D, int G, bool SPLIT>
 const void *fast_kernel() {
-    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, kNC, SPLIT>);
+    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, nc_of<KV>(), SPLIT>);
 }
 
 template <typename KV, int D, bool SPLIT>
@@ -478,12 +492,13 @@ int run_v2(const V2 &p) {
         const bool quant = p.kv_dtype == GOLLEK_DTYPE_I8;
         const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * kSlabBytes;
         const int max_ctas = sm_count(dev) * 2;
-        DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, kNC, 0, p.S, max_ctas);
+        const int nc = nc_for(p.kv_dtype);
+        DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, nc, 0, p.S, max_ctas);
         int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) /
-                                   (2 * tile * kNC));
+                                   (2 * tile * nc));
         spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
-        const int stages = spw * kNC;
-        DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, kNC, stages, p.S, max_ctas);
+        const int stages = spw * nc;
+        DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, nc, stages, p.S, max_ctas);
         if (L.total > 227 * 1024) fn = nullptr;
         if (fn) {
             void *ws = nullptr;
@@ -506,12 +521,12 @@ int run_v2(const V2 &p) {
             GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
                     "cudaFuncSetAttribute");
             int per_sm = 0;
-            GK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, (kNC + 1) * 32, L.total),
+            GK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, (nc + 1) * 32, L.total),
                     "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
             if (per_sm < 1) per_sm = 1;
             const int grid = std::min(sm_count(dev) * per_sm, max_ctas);  // smem sized for max_ctas
             void *args[] = {&tmk, &tmv, &a};
-            GK_CUDA(cudaLaunchKernel(fn, dim3(grid), dim3((kNC + 1) * 32), args, L.total, st),
+            GK_CUDA(cudaLaunchKernel(fn, dim3(grid), dim3((nc + 1) * 32), args, L.total, st),
                     "decode_tma_kernel launch");
             return GOLLEK_OK;
         }
