@@ -40,6 +40,13 @@ SIGNATURES = {
                                            _c_int, _c_ll, _c_ll, _c_ll, _c_float, _c_float, _c_int,
                                            _vp, _c_size, _vp]),
     "gollek_paged_attention_workspace_size": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
+    "gollek_paged_attention_prefill": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int,
+                                                _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                                _c_int, _c_ll, _c_int, _c_int, _c_ll, _c_ll, _c_ll,
+                                                _c_float, _c_float, _c_int, _c_int, _vp, _c_size,
+                                                _vp]),
+    "gollek_paged_attention_prefill_workspace_size": (_c_size, [_c_int, _c_int, _c_int, _c_int,
+                                                                _c_int]),
     "gollek_paged_attention_v2_noalloc": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int,
                                                    _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                                    _c_ll, _c_int, _c_int, _c_ll, _c_ll, _c_ll,

@@ -21,7 +21,10 @@ constexpr int kMaxFastSeqs = 16384;
 constexpr int kMinRunGroups = 8;   // smallest per-CTA range, in groups
 // Cost of starting a run (a q load, a merge of the warp states, maybe a split-K
 // exchange), in 16-token groups; CTAs are balanced on groups + kRunCost per run.
-constexpr int kRunCost = 16;
+#ifndef GK_RUN_COST
+#define GK_RUN_COST 16
+#endif
+constexpr int kRunCost = GK_RUN_COST;
 
 struct DecodeArgs {
     void *out;
@@ -40,6 +43,7 @@ struct DecodeArgs {
     int num_stages;       // stage ring length (tensor-memory kernel: K tiles)
     int num_vstages;      // tensor-memory kernel: V tiles
     int box3d;            // 1: one 3-D TMA box (all 128-byte slabs of 16 rows) per page
+    int seq_div;          // block-table row of sequence s is s / seq_div (queries of one sequence)
     int scale_mode;       // int8: 0 per-token scales by bulk copy, 1 one scale per page, 2 general
     float q_scale;        // applied to q when staged: scale*log2(e), or scale with soft-cap
     float soft_cap;       // > 0: cap*tanh(score/cap)

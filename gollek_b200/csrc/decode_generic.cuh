@@ -29,6 +29,7 @@ struct GenericArgs {
     long long scale_page_stride, scale_head_stride, scale_token_stride;
     int num_q_heads, num_kv_heads, head_dim, block_size, max_blocks, num_blocks;
     int window, q_bf16, kv_dtype;
+    int seq_div;  // block-table row of sequence s is s / seq_div
     float q_scale, soft_cap, post_scale, norm_eps;
 };
 
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kGenWarps * 32) decode_generic_kernel(const Ge
 
     const bool quant = a.kv_dtype == GOLLEK_DTYPE_I8 || a.kv_dtype == GOLLEK_DTYPE_I4;
     for (int t = win_start + warp; t < len; t += kGenWarps) {
-        int page = a.block_tables[static_cast<long long>(s) * a.max_blocks + t / BS];
+        int page = a.block_tables[static_cast<long long>(s / a.seq_div) * a.max_blocks + t / BS];
         if (page < 0 || (a.num_blocks > 0 && page >= a.num_blocks)) {
             if (lane == 0) raise_status(GOLLEK_STATUS_BAD_BLOCK_ID);
             continue;

@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int p_first = t0 / a.block_size;
                 l.row_off = a.block_size < kRows ? 0 : t0 % a.block_size;
                 const int pages_in_seq = (len + a.block_size - 1) / a.block_size;
-                const int *bt = a.block_tables + static_cast<long long>(t.r.s) * a.max_blocks;
+                const int *bt = a.block_tables + static_cast<long long>(t.r.s / a.seq_div) * a.max_blocks;
                 for (int j = 0; j < npg; ++j) {
                     const int pg = p_first + j;
                     if (pg < pages_in_seq && (pg + 1) * a.block_size > ws) {

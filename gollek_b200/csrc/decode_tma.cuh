@@ -37,6 +37,10 @@
 
 #include "decode_common.cuh"
 
+#ifndef GK_POLL_SLEEP_NS
+#define GK_POLL_SLEEP_NS 20  // producer's sleep between polls of busy stages
+#endif
+
 namespace gk {
 
 template <typename KV>
@@ -306,7 +310,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             const int p_first = q.t0 / a.block_size;
             q.row_off = a.block_size < kRows ? 0 : q.t0 % a.block_size;
             const int pages_in_seq = (len + a.block_size - 1) / a.block_size;
-            const int *bt = a.block_tables + static_cast<long long>(r.s) * a.max_blocks;
+            const int *bt = a.block_tables + static_cast<long long>(r.s / a.seq_div) * a.max_blocks;
             q.pid0 = q.pid1 = 0;
             q.loaded = 0;
             for (int j = 0; j < npg; ++j) {
@@ -449,7 +453,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     }
                     break;
                 }
-                __nanosleep(20);
+#if GK_POLL_SLEEP_NS > 0
+                __nanosleep(GK_POLL_SLEEP_NS);
+#endif
             }
             xw = xn;
             gbase = gn;

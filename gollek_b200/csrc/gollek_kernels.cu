@@ -113,8 +113,9 @@ int sm_count(int dev) {
     return n;
 }
 
-// Library-owned split-K scratch for (device, stream), zero-filled when (re)allocated.
-int library_workspace(int dev, void *stream, size_t bytes, void **out) {
+// Library-owned split-K scratch for (device, stream), zero-filled when (re)allocated;
+// *cap_out receives its size.
+int library_workspace(int dev, void *stream, size_t bytes, void **out, size_t *cap_out = nullptr) {
     const size_t tkey = stream == static_cast<void *>(cudaStreamPerThread)
                             ? std::hash<std::thread::id>()(std::this_thread::get_id())
                             : 0;
@@ -133,6 +134,7 @@ int library_workspace(int dev, void *stream, size_t bytes, void **out) {
         slot = {p, bytes};
     }
     *out = slot.first;
+    if (cap_out) *cap_out = slot.second;
     return GOLLEK_OK;
 }
 
@@ -150,15 +152,40 @@ int dtype_bytes(int dt) {
     }
 }
 
-size_t ws_counters_bytes(int S, int Hkv) {
-    return align_up(static_cast<uint32_t>(S) * Hkv * 4u, 256u);
-}
+// Split-K scratch of W bytes: the arrival counters (int per (sequence, kv-head), zero
+// between calls) fill the first W/128 bytes, the partial states follow.  The counter
+// region depends on W alone, so one workspace can serve calls of any sizes: no call's
+// partials ever land where another call's counters live.  Every call that fits in W has
+// its counters inside the region (each (sequence, kv-head) needs >= 64 * 12 bytes of
+// partials for its 4-byte counter).
+size_t ws_counter_region(size_t W) { return (W / 128 + 255) / 256 * 256; }
 
-size_t ws_bytes(int S, int Hq, int Hkv, int D) {
+size_t ws_partials_bytes(int S, int Hq, int Hkv, int D) {
     const int G = Hq / Hkv;
     const size_t slot = static_cast<size_t>(2 * G + G * D) * 4;
-    return ws_counters_bytes(S, Hkv) + static_cast<size_t>(S) * Hkv * kMaxSplits * slot;
+    return static_cast<size_t>(S) * Hkv * kMaxSplits * slot;
 }
+
+// Smallest W with ws_counter_region(W) + partials <= W.
+size_t ws_bytes(int S, int Hq, int Hkv, int D) {
+    const size_t P = ws_partials_bytes(S, Hq, Hkv, D);
+    return P + P / 64 + 1024;
+}
+
+// Multi-query attention as decode: query i of sequence s (absolute position
+// ctx[s] - Tq + i, PagedAttentionVectorAPI.compute) becomes sequence s*Tq + i with
+// context length ctx[s] - Tq + i + 1 when causal, ctx[s] otherwise.
+__global__ void prefill_lengths_kernel(const int *ctx, int *lens, int S, int Tq, int causal) {
+    const long long n = static_cast<long long>(S) * Tq;
+    for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < n;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int s = static_cast<int>(v / Tq), i = static_cast<int>(v % Tq);
+        const int c = ctx[s];
+        lens[v] = (causal && c >= 0) ? max(0, c - Tq + i + 1) : c;  // negative stays: BAD_POSITION
+    }
+}
+
+size_t prefill_lens_bytes(long long n) { return align_up(static_cast<uint32_t>(n * 4), 256u); }
 
 // ------------------------------------------------------------------ fast path
 
@@ -250,6 +277,7 @@ struct V2 {
     void *workspace;
     size_t workspace_bytes;
     void *stream;
+    int seq_div;  // > 1: S counts (sequence, query) pairs, block-table row = s / seq_div
 };
 
 int encode_map(CUtensorMap *m, const void *base, int kv, int D, long long rows, int box_rows) {
@@ -329,16 +357,18 @@ const void *fast_eligible(const V2 &p, int G, long long page_stride) {
     return pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32);
 }
 
-// Split-K scratch: the caller's workspace, or the library's per (device, stream) one.
-int v2_workspace(const V2 &p, int dev, void **ws) {
+// Split-K scratch: the caller's workspace, or the library's per (device, stream) one;
+// *cap receives its size (which fixes where the partials start).
+int v2_workspace(const V2 &p, int dev, void **ws, size_t *cap) {
     *ws = p.workspace;
+    *cap = p.workspace_bytes;
     const size_t need = ws_bytes(p.S, p.Hq, p.Hkv, p.D);
     if (*ws) {
         if (p.workspace_bytes < need)
             return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed", p.workspace_bytes, need);
         return GOLLEK_OK;
     }
-    return library_workspace(dev, p.stream, need, ws);
+    return library_workspace(dev, p.stream, need, ws, cap);
 }
 
 // 2-D tensor maps over the K and V pools: rows of head_dim elements, boxes of 128 bytes
@@ -353,7 +383,7 @@ int v2_maps(const V2 &p, long long page_stride, CUtensorMap *tmk, CUtensorMap *t
     return rc;
 }
 
-DecodeArgs v2_args(const V2 &p, void *ws, long long page_stride, int stages) {
+DecodeArgs v2_args(const V2 &p, void *ws, size_t ws_cap, long long page_stride, int stages) {
     const bool cap = p.soft_cap > 0.f;
     DecodeArgs a;
     a.out = p.out;
@@ -363,7 +393,7 @@ DecodeArgs v2_args(const V2 &p, void *ws, long long page_stride, int stages) {
     a.block_tables = p.bt;
     a.context_lens = p.ctx;
     a.counters = static_cast<int *>(ws);
-    a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ws_counters_bytes(p.S, p.Hkv));
+    a.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + ws_counter_region(ws_cap));
     a.page_rows = page_stride / p.D;
     a.scale_page_stride = p.sps;
     a.scale_head_stride = p.shs;
@@ -378,6 +408,7 @@ DecodeArgs v2_args(const V2 &p, void *ws, long long page_stride, int stages) {
     a.num_stages = stages;
     a.num_vstages = 0;
     a.box3d = 0;
+    a.seq_div = p.seq_div > 1 ? p.seq_div : 1;
     a.scale_mode = 2;
     if (p.kv_dtype == GOLLEK_DTYPE_I8) {
         const int R = p.BS < kRows ? p.BS : kRows;
@@ -451,7 +482,8 @@ int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     }
     if (!nk) return kNotTaken;
     void *ws = nullptr;
-    int rc = v2_workspace(p, dev, &ws);
+    size_t ws_cap = 0;
+    int rc = v2_workspace(p, dev, &ws, &ws_cap);
     if (rc) return rc;
     const long long rows =
         p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page : (1LL << 31) - 8;
@@ -460,7 +492,7 @@ int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     rc = encode_map4(&tmk, p.k, rows, box_rows);
     if (!rc) rc = encode_map4(&tmv, p.v, rows, box_rows);
     if (rc) return rc;
-    DecodeArgs a = v2_args(p, ws, page_stride, nk);
+    DecodeArgs a = v2_args(p, ws, ws_cap, page_stride, nk);
     a.num_vstages = nv;
     GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
             "cudaFuncSetAttribute");
@@ -502,7 +534,8 @@ int run_v2(const V2 &p) {
         if (L.total > 227 * 1024) fn = nullptr;
         if (fn) {
             void *ws = nullptr;
-            int rc = v2_workspace(p, dev, &ws);
+            size_t ws_cap = 0;
+            int rc = v2_workspace(p, dev, &ws, &ws_cap);
             if (rc) return rc;
             CUtensorMap tmk, tmv;
             const bool box3d = p.BS >= kRows && p.D * eb >= 256;
@@ -515,7 +548,7 @@ int run_v2(const V2 &p) {
                 rc = v2_maps(p, page_stride, &tmk, &tmv);
             }
             if (rc) return rc;
-            DecodeArgs a = v2_args(p, ws, page_stride, stages);
+            DecodeArgs a = v2_args(p, ws, ws_cap, page_stride, stages);
             a.box3d = box3d ? 1 : 0;
 
             GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
@@ -558,6 +591,7 @@ int run_v2(const V2 &p) {
     g.window = p.window;
     g.q_bf16 = p.q_dtype == GOLLEK_DTYPE_BF16;
     g.kv_dtype = p.kv_dtype;
+    g.seq_div = p.seq_div > 1 ? p.seq_div : 1;
     g.q_scale = cap ? p.scale : p.scale * log2e;
     g.soft_cap = p.soft_cap;
     g.post_scale = cap ? log2e : 1.f;
@@ -756,6 +790,92 @@ size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_heads, int 
     return ws_bytes(num_seqs, num_q_heads, num_kv_heads, head_dim);
 }
 
+size_t gollek_paged_attention_prefill_workspace_size(int num_seqs, int num_queries, int num_q_heads,
+                                                     int num_kv_heads, int head_dim) {
+    if (num_seqs <= 0 || num_queries <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 ||
+        head_dim <= 0 || static_cast<long long>(num_seqs) * num_queries > (1 << 30))
+        return 0;
+    const int n = num_seqs * num_queries;
+    return ws_bytes(n, num_q_heads, num_kv_heads, head_dim) + 2 * prefill_lens_bytes(n) + 512;
+}
+
+int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache, const void *v_cache,
+                                   const float *k_scales, const float *v_scales, const int *block_tables,
+                                   const int *context_lens, int num_seqs, int num_queries,
+                                   int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                                   int max_blocks_per_seq, int num_blocks, long long page_stride,
+                                   int q_dtype, int kv_dtype, long long scale_page_stride,
+                                   long long scale_head_stride, long long scale_token_stride,
+                                   float scale, float soft_cap, int sliding_window, int causal,
+                                   void *workspace, size_t workspace_bytes, void *stream) {
+    t_last_error.clear();
+    if (num_queries <= 0) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "num_queries %d < 1", num_queries);
+    if (num_seqs < 0 || static_cast<long long>(num_seqs) * num_queries > (1 << 30))
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT, "num_seqs * num_queries out of range");
+    if (!causal && sliding_window > 0 && num_queries > 1)
+        return fail(GOLLEK_ERR_UNSUPPORTED,
+                    "a sliding window without causal masking over several queries");
+    if (!context_lens) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    const int n = num_seqs * num_queries;
+    V2 p{};
+    p.out = out;
+    p.q = q;
+    p.k = k_cache;
+    p.v = v_cache;
+    p.ks = k_scales;
+    p.vs = v_scales;
+    p.bt = block_tables;
+    p.ctx = context_lens;  // checked below, replaced by the per-query lengths
+    p.S = n;
+    p.Hq = num_q_heads;
+    p.Hkv = num_kv_heads;
+    p.D = head_dim;
+    p.BS = block_size;
+    p.maxB = max_blocks_per_seq;
+    p.num_blocks = num_blocks;
+    p.page_stride = page_stride;
+    p.q_dtype = q_dtype;
+    p.kv_dtype = kv_dtype;
+    p.sps = scale_page_stride;
+    p.shs = scale_head_stride;
+    p.sts = scale_token_stride;
+    p.scale = scale;
+    p.soft_cap = soft_cap;
+    p.window = sliding_window;
+    p.norm_eps = 1e-9f;  // AttentionOnlineSoftmax.NORMALIZER_EPSILON
+    p.stream = stream;
+    p.seq_div = num_queries;
+    int rc = check_v2(p);
+    if (rc) return rc;
+    if (n == 0) return GOLLEK_OK;
+    int dev = 0;
+    GK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+    // [counters][partials] ... [per-query lengths at the end]
+    const size_t lens_bytes = prefill_lens_bytes(n);
+    const size_t need = ws_bytes(n, num_q_heads, num_kv_heads, head_dim) + 2 * lens_bytes + 512;
+    void *ws = workspace;
+    size_t cap = workspace_bytes;
+    if (ws) {
+        if (workspace_bytes < need)
+            return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
+    } else {
+        rc = library_workspace(dev, stream, need, &ws, &cap);
+        if (rc) return rc;
+    }
+    if (ws_counter_region(cap) + ws_partials_bytes(n, num_q_heads, num_kv_heads, head_dim) + lens_bytes > cap)
+        return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes too small", cap);
+    int *lens = reinterpret_cast<int *>(static_cast<uint8_t *>(ws) + (cap - lens_bytes) / 256 * 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int threads = 256;
+    const int blocks = static_cast<int>(std::min<long long>((n + threads - 1) / threads, 4096));
+    prefill_lengths_kernel<<<blocks, threads, 0, st>>>(context_lens, lens, num_seqs, num_queries, causal);
+    GK_CUDA(cudaGetLastError(), "prefill_lengths_kernel launch");
+    p.ctx = lens;
+    p.workspace = ws;
+    p.workspace_bytes = cap;
+    return run_v2(p);
+}
+
 int gollek_paged_attention_v2_noalloc(void *out, const void *q, const void *k_cache,
                                       const void *v_cache, const float *k_scales,
                                       const float *v_scales, const int *block_tables,
@@ -810,7 +930,8 @@ int gollek_paged_attention_v2_noalloc(void *out, const void *q, const void *k_ca
     if (rc) return rc;
     // The arrival counters must start at zero; a previous call leaves them zeroed unless
     // it gave up half way, so clear them on every call.
-    GK_CUDA(cudaMemsetAsync(scratch, 0, ws_counters_bytes(p.S, p.Hkv), static_cast<cudaStream_t>(stream)),
+    GK_CUDA(cudaMemsetAsync(scratch, 0, align_up(static_cast<uint32_t>(p.S) * p.Hkv * 4u, 256u),
+                            static_cast<cudaStream_t>(stream)),
             "cudaMemsetAsync(no-alloc scratch counters)");
     p.workspace = scratch;
     p.workspace_bytes = GOLLEK_NOALLOC_SCRATCH_BYTES;

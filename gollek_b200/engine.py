@@ -201,23 +201,33 @@ def update_cache(key, value, session: KVCacheSession, layer_idx: int, start_pos:
 
 def paged_attention_compute(q, session: KVCacheSession, layer_idx: int, total_tokens: int,
                             num_q_heads: int, num_kv_heads: int, head_dim: int, scale: float,
-                            soft_cap: float = 0.0, sliding_window: int = 0, out=None):
-    """PagedAttentionVectorAPI.compute (attention/PagedAttentionVectorAPI.java:60-180) for one
-    decode token: q [1, 1, num_q_heads, head_dim] (fp32 or bf16) attends to the layer's
-    first total_tokens positions.  Returns [1, 1, num_q_heads, head_dim]."""
+                            soft_cap: float = 0.0, sliding_window: int = 0, out=None,
+                            causal: bool = True):
+    """PagedAttentionVectorAPI.compute (attention/PagedAttentionVectorAPI.java:60-180):
+    q [1, Tq, num_q_heads, head_dim] (fp32 or bf16), query i at position
+    total_tokens - Tq + i, attending to the layer's first total_tokens positions (up to its
+    own position when causal).  Returns [1, Tq, num_q_heads, head_dim]."""
     import torch
 
     from . import ops
-    if q.dim() != 4 or q.shape[1] != 1:
-        raise ValueError("decode attention takes one query token per sequence")
+    if q.dim() != 4 or q.shape[0] != 1:
+        raise ValueError("q must be [1, Tq, num_q_heads, head_dim]")
     bm = session.block_manager
     table = session.block_table_tensor(layer_idx)
     ctx = torch.tensor([total_tokens], dtype=torch.int32, device=q.device)
-    res = ops.paged_attention(q.reshape(q.shape[0], num_q_heads, head_dim).contiguous(), bm.k_slab,
-                              bm.v_slab, table, ctx, num_kv_heads=num_kv_heads,
-                              block_size=session.tokens_per_block, scale=scale,
-                              num_blocks=bm.max_blocks, soft_cap=soft_cap,
-                              sliding_window=sliding_window, **_kv_args(bm))
+    if q.shape[1] == 1:
+        res = ops.paged_attention(q.reshape(1, num_q_heads, head_dim).contiguous(), bm.k_slab,
+                                  bm.v_slab, table, ctx, num_kv_heads=num_kv_heads,
+                                  block_size=session.tokens_per_block, scale=scale,
+                                  num_blocks=bm.max_blocks, soft_cap=soft_cap,
+                                  sliding_window=sliding_window, **_kv_args(bm))
+    else:
+        res = ops.paged_attention_prefill(q.contiguous(), bm.k_slab, bm.v_slab, table, ctx,
+                                          num_kv_heads=num_kv_heads,
+                                          block_size=session.tokens_per_block, scale=scale,
+                                          causal=causal, num_blocks=bm.max_blocks,
+                                          soft_cap=soft_cap, sliding_window=sliding_window,
+                                          **_kv_args(bm))
     res = res.reshape(q.shape)
     if out is not None:
         out.copy_(res)

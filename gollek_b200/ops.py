@@ -79,6 +79,31 @@ def paged_attention(q, k_cache, v_cache, block_tables, context_lens, *, num_kv_h
     return out
 
 
+def paged_attention_prefill(q, k_cache, v_cache, block_tables, context_lens, *, num_kv_heads,
+                            block_size, scale=None, causal=True, num_blocks=0, page_stride=0,
+                            k_scales=None, v_scales=None, scale_strides=(0, 0, 0), soft_cap=0.0,
+                            sliding_window=0, int4=False, out=None, workspace=None, stream=None):
+    """Multi-query attention (gollek_paged_attention_prefill): q [S, Tq, Hq, D]; the Tq
+    queries of sequence s sit at positions context_lens[s] - Tq .. context_lens[s] - 1."""
+    _require_cuda(q, k_cache, v_cache, block_tables, context_lens, k_scales, v_scales, out)
+    S, Tq, Hq, D = q.shape
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty_like(q)
+    sps, shs, sts = scale_strides
+    rc = _lib.load().gollek_paged_attention_prefill(
+        _ptr(out), _ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k_scales), _ptr(v_scales),
+        _ptr(block_tables), _ptr(context_lens), S, Tq, Hq, int(num_kv_heads), D, int(block_size),
+        block_tables.shape[1], int(num_blocks), int(page_stride), _TORCH_DTYPE[q.dtype],
+        kv_dtype_code(k_cache, int4), int(sps), int(shs), int(sts), float(scale),
+        float(soft_cap), int(sliding_window), int(bool(causal)), _ptr(workspace),
+        0 if workspace is None else workspace.numel() * workspace.element_size(),
+        _stream(q, stream))
+    check(rc)
+    return out
+
+
 def paged_attention_launch(out, q, k_cache, v_cache, block_tables, context_lens, scale):
     """The legacy fp32 entry point (synchronous): q/out [S,H,D], K/V [NB,H,BS,D]."""
     _require_cuda(out, q, k_cache, v_cache, block_tables, context_lens)

@@ -141,6 +141,37 @@ GOLLEK_API size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_
                                              int head_dim);
 
 /*
+ * Multi-query paged attention (several new tokens per sequence: prefill chunks,
+ * speculative verification).  Replaces PagedAttentionVectorAPI.compute with
+ * seqLenQ = num_queries > 1 (ST/generation/attention/PagedAttentionVectorAPI.java:60-180;
+ * query i at absolute position startPos + i = ctx[s] - num_queries + i, :77-78, and the
+ * causal / window bounds of computePagedHeadQuery, :126-180), which the PD service reaches
+ * through runPrefillAttention (PD/PrefillDecodeDisaggService.java:359-373).
+ *   q, out        [num_seqs][num_queries][num_q_heads][head_dim] (q_dtype)
+ *   context_lens  [num_seqs] total tokens including the num_queries new ones
+ *   causal        1: query i attends positions <= its own; 0: all context_lens[s] tokens
+ *   sliding_window  > 0: the last sliding_window positions up to the query (causal only
+ *                 when num_queries > 1; otherwise GOLLEK_ERR_UNSUPPORTED)
+ *   workspace     >= gollek_paged_attention_prefill_workspace_size(...), or NULL
+ * Every other argument as gollek_paged_attention_v2.  Each query reads its context once
+ * (queries of one sequence run back to back, so most repeats are served from L2).
+ */
+GOLLEK_API int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache,
+                                   const void *v_cache, const float *k_scales, const float *v_scales,
+                                   const int *block_tables, const int *context_lens, int num_seqs,
+                                   int num_queries, int num_q_heads, int num_kv_heads, int head_dim,
+                                   int block_size, int max_blocks_per_seq, int num_blocks,
+                                   long long page_stride, int q_dtype, int kv_dtype,
+                                   long long scale_page_stride, long long scale_head_stride,
+                                   long long scale_token_stride, float scale, float soft_cap,
+                                   int sliding_window, int causal, void *workspace,
+                                   size_t workspace_bytes, void *stream);
+
+/* Bytes of scratch gollek_paged_attention_prefill needs for these sizes. */
+GOLLEK_API size_t gollek_paged_attention_prefill_workspace_size(int num_seqs, int num_queries,
+                                                     int num_q_heads, int num_kv_heads, int head_dim);
+
+/*
  * Decode attention that allocates nothing.  No counterpart in the reference: this entry
  * point exists for callers that cannot allocate device memory themselves -- a caller
  * running inside a CUDA graph being captured elsewhere, a real-time or embedded host that

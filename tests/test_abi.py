@@ -72,6 +72,19 @@ def test_invalid_arguments_rejected_without_a_device(lib):
     assert rc == _lib.ERR_INVALID_ARGUMENT  # src_v NULL but dst_v set
 
 
+def test_prefill_arguments_rejected_without_a_device(lib):
+    d = ctypes.c_void_p(16)
+    args = lambda tq, window, causal: (d, d, d, d, None, None, d, d, 2, tq, 8, 8, 128, 16, 4, 0, 0,
+                                       _lib.F32, _lib.F32, 0, 0, 0, 0.1, 0.0, window, causal, None,
+                                       0, None)
+    assert lib.gollek_paged_attention_prefill(*args(0, 0, 1)) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.gollek_paged_attention_prefill(*args(4, 32, 0)) == _lib.ERR_UNSUPPORTED
+    assert b"causal" in lib.gollek_last_error_string()
+    n = lib.gollek_paged_attention_prefill_workspace_size(4, 8, 32, 8, 128)
+    assert n >= lib.gollek_paged_attention_workspace_size(32, 32, 8, 128) + 32 * 4
+    assert lib.gollek_paged_attention_prefill_workspace_size(4, 0, 32, 8, 128) == 0
+
+
 def test_workspace_size_is_host_arithmetic(lib):
     n = lib.gollek_paged_attention_workspace_size(64, 32, 8, 128)
     slot = (2 * 4 + 4 * 128) * 4

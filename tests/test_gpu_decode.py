@@ -511,3 +511,24 @@ def test_bf16_nan_outside_the_context(cuda_device, monkeypatch, path):
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all()
     np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("own_workspace", [True, False])
+def test_workspace_reuse_across_batch_sizes(cuda_device, own_workspace):
+    """One split-K workspace serving calls of different batch sizes in turn: the arrival
+    counters of a larger batch must not land on partials a smaller batch left behind."""
+    from gollek_b200 import _lib, ops
+    lib = _lib.load()
+    big = lib.gollek_paged_attention_workspace_size(24, 32, 8, 128)
+    ws = torch.zeros(big, dtype=torch.uint8, device=cuda_device) if own_workspace else None
+    rng = np.random.default_rng(71)
+    for S in (3, 24, 3, 17, 5, 24):
+        ctx = rng.integers(3000, 9000, S).tolist()  # few long sequences: split across CTAs
+        q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=S, kv_std=0.5)
+        qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
+        want = oracle_decode(qb, kb, vb, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16)
+        out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kb, cuda_device, torch.bfloat16),
+                                  _t(vb, cuda_device, torch.bfloat16), _t(bt, cuda_device),
+                                  _t(ctx, cuda_device), num_kv_heads=8, block_size=16,
+                                  num_blocks=k.shape[0], workspace=ws)
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0, err_msg=f"S={S}")

@@ -1,0 +1,111 @@
+"""Multi-query paged attention (gollek_paged_attention_prefill) against the oracle's
+restatement of PagedAttentionVectorAPI.compute with seqLenQ > 1 (causal / non-causal,
+sliding window, soft-cap; fp32, bf16 and int8 KV), through the C ABI.
+
+Tolerances as for decode: fp32 <= 1e-4 relative to the output scale; bf16 / int8 KV
+<= 2e-2 absolute against the fp32 oracle on the same rounded inputs.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.helpers import decode_case, quantize_rows_int8
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _t(x, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def _case(ctx, tq, hq, hkv, seed, bs=16):
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=128, bs=bs, seed=seed, kv_std=0.5)
+    rng = np.random.default_rng(seed + 1)
+    qm = rng.standard_normal((len(ctx), tq, hq, 128)).astype(np.float32)
+    return qm, k, v, bt, ctx
+
+
+def _oracle(q, k, v, bt, ctx, scale, *, hkv, bs, causal, window=0, soft_cap=0.0, storage=O.FP32,
+            ks=None, vs=None):
+    return O.a2_compute(q, k, v, bt, ctx, scale, storage=storage, num_kv_heads=hkv, block_size=bs,
+                        k_scale=ks, v_scale=vs, causal=causal, soft_cap=soft_cap,
+                        sliding_window=window, threads=O.num_threads())
+
+
+@pytest.mark.parametrize("tq,causal,window,soft_cap", [(1, 1, 0, 0.0), (4, 1, 0, 0.0), (8, 1, 0, 0.0),
+                                                       (5, 0, 0, 0.0), (6, 1, 64, 0.0), (3, 1, 0, 30.0)])
+def test_prefill_bf16(cuda_device, tq, causal, window, soft_cap):
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([3, 17, 300, 2100, 6000], tq, 32, 8, seed=50 + tq)
+    qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(qb, kb, vb, bt, ctx, scale, hkv=8, bs=16, causal=causal, window=window,
+                   soft_cap=soft_cap)
+    for _ in range(2):
+        out = ops.paged_attention_prefill(_t(qb, cuda_device, torch.bfloat16),
+                                          _t(kb, cuda_device, torch.bfloat16),
+                                          _t(vb, cuda_device, torch.bfloat16), _t(bt, cuda_device),
+                                          _t(ctx, cuda_device), num_kv_heads=8, block_size=16,
+                                          scale=scale, causal=bool(causal), num_blocks=k.shape[0],
+                                          sliding_window=window, soft_cap=soft_cap)
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+    assert ops.device_status(cuda_device.index or 0) == 0
+
+
+def test_prefill_fp32_gqa8(cuda_device):
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([40, 129, 777], 4, 64, 8, seed=61)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(q, k, v, bt, ctx, scale, hkv=8, bs=16, causal=1)
+    out = ops.paged_attention_prefill(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                                      _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8,
+                                      block_size=16, scale=scale, num_blocks=k.shape[0])
+    got = out.cpu().numpy()
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
+
+
+def test_prefill_int8_reference_scales(cuda_device):
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([9, 250, 1500], 3, 32, 8, seed=62)
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    qb = O.round_bf16(q)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(qb, kq, vq, bt, ctx, scale, hkv=8, bs=16, causal=1, storage=O.INT8, ks=ks, vs=vs)
+    out = ops.paged_attention_prefill(_t(qb, cuda_device, torch.bfloat16), _t(kq, cuda_device),
+                                      _t(vq, cuda_device), _t(bt, cuda_device), _t(ctx, cuda_device),
+                                      num_kv_heads=8, block_size=16, scale=scale,
+                                      num_blocks=k.shape[0], k_scales=_t(ks, cuda_device),
+                                      v_scales=_t(vs, cuda_device), scale_strides=(8 * 16, 16, 1))
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+def test_prefill_more_queries_than_context(cuda_device):
+    """Sequences shorter than the query count: queries before the first position see
+    nothing and come out as zeros, as in the reference (no token passes the causal bound)."""
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([2, 5, 40], 6, 16, 8, seed=63)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(q, k, v, bt, ctx, scale, hkv=8, bs=16, causal=1)
+    out = ops.paged_attention_prefill(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                                      _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8,
+                                      block_size=16, scale=scale, num_blocks=k.shape[0])
+    got = out.cpu().numpy()
+    assert np.abs(got - want).max() <= 1e-4 * max(np.abs(want).max(), 1e-6)
+    assert not got[0, :4].any() and not got[1, :1].any()
+
+
+def test_prefill_refuses_window_without_causal(cuda_device):
+    from gollek_b200 import _lib, ops
+    q, k, v, bt, ctx = _case([40], 2, 8, 8, seed=64)
+    with pytest.raises(_lib.GollekError) as e:
+        ops.paged_attention_prefill(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                                    _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8,
+                                    block_size=16, causal=False, sliding_window=16,
+                                    num_blocks=k.shape[0])
+    assert e.value.code == _lib.ERR_UNSUPPORTED
