@@ -173,7 +173,7 @@ class DecodeBatch:
         qo = 2 * self.q.numel() * self.q_elem
         return kv + scales + qo + pages * 4 + len(self.ctx_np) * 4
 
-    def run(self, out=None, q=None, bt=None, ctx=None, stream=None):
+    def run(self, out=None, q=None, bt=None, ctx=None, stream=None, workspace=None):
         from gollek_b200 import ops
         return ops.paged_attention(q if q is not None else self.q, self.k, self.v,
                                    bt if bt is not None else self.bt,
@@ -181,7 +181,8 @@ class DecodeBatch:
                                    num_kv_heads=self.hkv, block_size=self.sh["bs"],
                                    num_blocks=self.nb, k_scales=self.k_scales,
                                    v_scales=self.v_scales, scale_strides=self.scale_strides,
-                                   out=out if out is not None else self.out, stream=stream)
+                                   out=out if out is not None else self.out, stream=stream,
+                                   workspace=workspace)
 
 
 # ------------------------------------------------------------------ clocks
@@ -387,54 +388,76 @@ def bench_decode(args, world, rank, local):
     # ---------------- e2e: host buffers in, host result out, through the C ABI
     from gollek_b200 import _lib
     B, Hq, D = batch.q.shape
-    hq_pin = batch.q.cpu().pin_memory()
-    hbt_pin = batch.bt.cpu().pin_memory()
-    hctx_pin = batch.ctx.cpu().pin_memory()
-    hout_pin = torch.empty(batch.out.shape, dtype=batch.out.dtype).pin_memory()
     append = args.workload in ("decode_bf16", "decode_fp32", "longctx")
+    # The step's host inputs sit in one pinned staging block (q, tables, lengths and, with
+    # the append, the new K/V rows and their positions), so a step moves them with one
+    # H2D copy; the output comes back with one D2H copy.
+    parts = [("q", batch.q.cpu()), ("bt", batch.bt.cpu()), ("ctx", batch.ctx.cpu())]
     if append:
         g = torch.Generator().manual_seed(args.seed + 7)
         kv_dt = batch.k.dtype
-        hk_new = torch.randn((B, batch.hkv, D), generator=g).to(kv_dt).pin_memory()
-        hv_new = torch.randn((B, batch.hkv, D), generator=g).to(kv_dt).pin_memory()
-        hpos = (batch.ctx.cpu() - 1).to(torch.int32).pin_memory()
-    dq, dbt, dctx = torch.empty_like(batch.q), torch.empty_like(batch.bt), torch.empty_like(batch.ctx)
-    if append:
-        dk_new = torch.empty((B, batch.hkv, D), dtype=batch.k.dtype, device=dev)
-        dv_new = torch.empty_like(dk_new)
-        dpos = torch.empty((B,), dtype=torch.int32, device=dev)
+        parts += [("k_new", torch.randn((B, batch.hkv, D), generator=g).to(kv_dt)),
+                  ("v_new", torch.randn((B, batch.hkv, D), generator=g).to(kv_dt)),
+                  ("pos", (batch.ctx.cpu() - 1).to(torch.int32))]
+    offs, total = {}, 0
+    for name, t in parts:
+        offs[name] = total
+        total += (t.numel() * t.element_size() + 255) // 256 * 256
+    h_stage = torch.empty(total, dtype=torch.uint8).pin_memory()
+    d_stage = torch.empty(total, dtype=torch.uint8, device=dev)
+
+    def view(buf, name, like):
+        n = like.numel() * like.element_size()
+        return buf[offs[name]:offs[name] + n].view(like.dtype).view(like.shape)
+
+    for name, t in parts:
+        view(h_stage, name, t).copy_(t)
+    d = {name: view(d_stage, name, t) for name, t in parts}
+    hout_pin = torch.empty(batch.out.shape, dtype=batch.out.dtype).pin_memory()
+    ws_e2e = torch.zeros(_lib.load().gollek_paged_attention_workspace_size(B, Hq, batch.hkv, D),
+                         dtype=torch.uint8, device=dev)
 
     def e2e_step():
-        dq.copy_(hq_pin, non_blocking=True)
-        dbt.copy_(hbt_pin, non_blocking=True)
-        dctx.copy_(hctx_pin, non_blocking=True)
+        d_stage.copy_(h_stage, non_blocking=True)
         if append:
-            dk_new.copy_(hk_new, non_blocking=True)
-            dv_new.copy_(hv_new, non_blocking=True)
-            dpos.copy_(hpos, non_blocking=True)
-            ops.kv_append(dk_new, dv_new, dpos, dbt, batch.k, batch.v, block_size=batch.sh["bs"],
-                          num_blocks=batch.nb)
-        batch.run(q=dq, bt=dbt, ctx=dctx)
+            ops.kv_append(d["k_new"], d["v_new"], d["pos"], d["bt"], batch.k, batch.v,
+                          block_size=batch.sh["bs"], num_blocks=batch.nb)
+        batch.run(q=d["q"], bt=d["bt"], ctx=d["ctx"], workspace=ws_e2e)
         hout_pin.copy_(batch.out, non_blocking=True)
+
+    # The step (copy in, append, decode, copy out) replays as one CUDA graph when it
+    # captures; otherwise it runs eagerly.
+    e2e_graph, graph_note = None, "eager"
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    try:
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_graph, graph_note = cg, "CUDA graph of the step"
+    except Exception as exc:  # capture refused: run the same calls eagerly
+        torch.cuda.synchronize()
+        graph_note = f"eager (graph capture failed: {str(exc)[:80]})"
+    step_fn = e2e_graph.replay if e2e_graph is not None else e2e_step
 
     e2e_steps = max(1, min(args.steps, 100))
     for _ in range(args.warmup):
-        e2e_step()
+        step_fn()
     torch.cuda.synchronize()
     barrier(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
     f0.record(stream)
     for _ in range(e2e_steps):
-        e2e_step()
+        step_fn()
     f1.record(stream)
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
     barrier(world)
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
-    h2d = (hq_pin.numel() * hq_pin.element_size() + hbt_pin.numel() * 4 + hctx_pin.numel() * 4)
-    if append:
-        h2d += 2 * hk_new.numel() * hk_new.element_size() + hpos.numel() * 4
+    h2d = h_stage.numel()
     d2h = hout_pin.numel() * hout_pin.element_size()
 
     if args.workload == "longctx":
@@ -500,11 +523,13 @@ def bench_decode(args, world, rank, local):
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "wall_s": wall,
-                    "path": "pinned host q/tables/lengths (+new K/V rows) -> H2D -> "
-                            "gollek_kv_append -> gollek_paged_attention_v2 -> D2H out"
+                    "path": "pinned host staging block (q, tables, lengths, new K/V rows) -> one H2D -> "
+                            "gollek_kv_append -> gollek_paged_attention_v2 -> one D2H of out"
                             if append else
-                            "pinned host q/tables/lengths -> H2D -> gollek_paged_attention_v2 -> D2H out",
-                    "gpu_launches_per_step": 2 if append else 1},
+                            "pinned host staging block (q, tables, lengths) -> one H2D -> "
+                            "gollek_paged_attention_v2 -> one D2H of out",
+                    "gpu_launches_per_step": 2 if append else 1,
+                    "execution": graph_note},
             "gpu_launches": launches,
             "clocks": clocks,
             "cpu_baseline": cpu,

@@ -532,3 +532,38 @@ def test_workspace_reuse_across_batch_sizes(cuda_device, own_workspace):
                                   _t(ctx, cuda_device), num_kv_heads=8, block_size=16,
                                   num_blocks=k.shape[0], workspace=ws)
         np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0, err_msg=f"S={S}")
+
+
+def test_decode_and_append_capture_in_a_cuda_graph(cuda_device):
+    """With a caller workspace, gollek_kv_append + gollek_paged_attention_v2 capture into a
+    CUDA graph (no allocation or synchronisation inside) and replays match eager calls."""
+    from gollek_b200 import _lib, ops
+    ctx = [100, 2000, 5000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=81, kv_std=0.5)
+    dev = cuda_device
+    qd = _t(O.round_bf16(q), dev, torch.bfloat16)
+    kd, vd = _t(O.round_bf16(k), dev, torch.bfloat16), _t(O.round_bf16(v), dev, torch.bfloat16)
+    btd, ctxd = _t(bt, dev), _t(ctx, dev)
+    new_k = torch.randn((3, 8, 128), device=dev).to(torch.bfloat16)
+    new_v = torch.randn((3, 8, 128), device=dev).to(torch.bfloat16)
+    pos = (ctxd - 1).to(torch.int32)
+    ws = torch.zeros(_lib.load().gollek_paged_attention_workspace_size(3, 32, 8, 128), dtype=torch.uint8,
+                     device=dev)
+    out = torch.empty_like(qd)
+
+    def step():
+        ops.kv_append(new_k, new_v, pos, btd, kd, vd, block_size=16, num_blocks=k.shape[0])
+        ops.paged_attention(qd, kd, vd, btd, ctxd, num_kv_heads=8, block_size=16, num_blocks=k.shape[0],
+                            out=out, workspace=ws)
+
+    step()
+    torch.cuda.synchronize()
+    eager = out.clone()
+    out.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(2):
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
