@@ -37,6 +37,9 @@
 
 #include "decode_common.cuh"
 
+#ifndef GK_WAVE
+#define GK_WAVE 32
+#endif
 #ifndef GK_POLL_SLEEP_NS
 #define GK_POLL_SLEEP_NS 20  // producer's sleep between polls of busy stages
 #endif
@@ -291,7 +294,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         // while the current wave waits and issues, so a wave starts with its ids ready.
         const int R = a.block_size < kRows ? a.block_size : kRows;  // rows per TMA box
         const int npg = kRows / R;                                  // pages per stage (<= 2)
-        const int W = NS < 32 ? NS : 32;
+        const int W = NS < GK_WAVE ? NS : GK_WAVE;  // groups per producer wave
         struct GroupLoc {
             int h, t0, row_off, pid0, pid1, stage, round, len, win_start;
             unsigned loaded;
