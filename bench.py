@@ -660,8 +660,39 @@ def bench_migrate(args, world, rank, local):
             "roofline": {"bound": "nvlink", "achieved": gbs, "peak": peak, "unit": "GB/s",
                          "frac": gbs / peak, "traffic": None,
                          "peak_source": "770 GB/s measured peer copy per direction per source GPU"},
-            "gpu_launches": args.steps * nsrc, "clocks": clk.summary(), "cpu_baseline": None,
+            "gpu_launches": args.steps * nsrc, "clocks": clk.summary(),
+            "cpu_baseline": None if args.no_cpu_baseline else cpu_migrate_baseline(args.seed),
         }), flush=True)
+
+
+def cpu_migrate_baseline(seed, seconds=3.0, sample_blocks=128):
+    """The reference's migration loop (transferKvToDecodePartition: per (block, layer)
+    copyFrom of 32 KiB slices, PD/PrefillDecodeDisaggService.java:415-429) restated in
+    oracle/oracle.c, timed single-threaded on host memory over a bounded sample of config
+    4's blocks (1 MiB per block for each of K and V) into a permuted destination layout."""
+    import numpy as np
+    from oracle import oracle as O
+    L, bpb = 32, 16 * 8 * 128 * 2
+    rng = np.random.default_rng(seed)
+    n = sample_blocks
+    src_k = np.frombuffer(rng.bytes(n * L * bpb), dtype=np.uint8).copy()
+    src_v = np.frombuffer(rng.bytes(n * L * bpb), dtype=np.uint8).copy()
+    dst_k, dst_v = np.zeros_like(src_k), np.zeros_like(src_v)
+    src = np.arange(n, dtype=np.int32)
+    dst = rng.permutation(n).astype(np.int32)
+    O.migrate(src_k, src_v, dst_k, dst_v, src, dst, L, bpb)  # warm the pages
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        moved = O.migrate(src_k, src_v, dst_k, dst_v, src, dst, L, bpb)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = moved * reps / el / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} blocks x 32 layers x 32 KiB for K and V ({moved / 2**30:.2f} GiB), "
+                      f"{reps} repetitions in {el:.1f} s, host memory to host memory; "
+                      "oracle/oracle.c oracle_migrate, the reference's sequential copy loop"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -675,8 +706,17 @@ def bench_reference(args):
     import numpy as np
     from oracle import oracle as O
     if args.workload == "migrate":
-        print(json.dumps({"impl": "reference", "unavailable": "migrate: the reference copies "
-                          "within one host pool; run --workload migrate for the GPU arm only"}))
+        r = cpu_migrate_baseline(args.seed, seconds=max(1.0, min(20.0, 2.0 * args.steps)))
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u8 (bf16 KV bytes)",
+            "data": "synthetic (seeded; BASELINE config 4 shapes)",
+            "config": {"workload": "config4_prefill_to_decode_migration", "layers": 32, "kv_heads": 8,
+                       "head_dim": 128, "block_size": 16},
+            "cpu_baseline": r,
+            "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
         return
 
     class HostBatch:
