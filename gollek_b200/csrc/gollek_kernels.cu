@@ -189,21 +189,6 @@ size_t prefill_lens_bytes(long long n) { return align_up(static_cast<uint32_t>(n
 
 // ------------------------------------------------------------------ fast path
 
-// Consumer warps per CTA (one CTA per SM), by KV type: the int8 and fp32 consumers are
-// latency-bound per group and gain from more warps; 16-bit KV keeps the registers for
-// its staged fragments.
-#ifndef GK_NC_I8
-#define GK_NC_I8 8
-#endif
-#ifndef GK_NC_F32
-#define GK_NC_F32 12
-#endif
-constexpr int kNC = 8;
-template <typename KV>
-constexpr int nc_of() {
-    return std::is_same<KV, int8_t>::value ? GK_NC_I8 : std::is_same<KV, float>::value ? GK_NC_F32 : kNC;
-}
-int nc_for(int kv) { return kv == GOLLEK_DTYPE_I8 ? GK_NC_I8 : kv == GOLLEK_DTYPE_F32 ? GK_NC_F32 : kNC; }
 constexpr uint32_t kSmemBudget = 224 * 1024;
 constexpr int kMaxStagesPerWarp = 6;
 
@@ -213,39 +198,69 @@ struct Launch {
     bool quant;
 };
 
-template <typename KV, int D, int G, bool SPLIT>
+// Consumer warps per CTA (one CTA per SM).  Nine, or twelve, warps in all put three on
+// one SM sub-partition, whose register file then caps a thread at 168 registers; thirteen
+// would cap it at 128 and spill.  16-bit KV compiles 8 and 7 consumer warps (the host
+// takes the one with more stages in flight: 7 when G = 8, whose per-warp merge buffers
+// crowd out stages), int8 and fp32 compile 11 and 8 (their consumers are latency-bound,
+// so 11 unless its stages do not fit).
+template <typename KV, int D, int G, int NC, bool SPLIT>
 const void *fast_kernel() {
-    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, nc_of<KV>(), SPLIT>);
+    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, NC, SPLIT>);
 }
 
-template <typename KV, int D, bool SPLIT>
+template <typename KV, int D, int NC, bool SPLIT>
 const void *pick_g(int G) {
     switch (G) {
-        case 1: return fast_kernel<KV, D, 1, SPLIT>();
-        case 2: return fast_kernel<KV, D, 2, SPLIT>();
-        case 4: return fast_kernel<KV, D, 4, SPLIT>();
-        case 8: return fast_kernel<KV, D, 8, SPLIT>();
+        case 1: return fast_kernel<KV, D, 1, NC, SPLIT>();
+        case 2: return fast_kernel<KV, D, 2, NC, SPLIT>();
+        case 4: return fast_kernel<KV, D, 4, NC, SPLIT>();
+        case 8: return fast_kernel<KV, D, 8, NC, SPLIT>();
         default: return nullptr;
     }
 }
 
+// Consumer-warp counts compiled for a KV type and head_dim, in preference order.
+struct NcList {
+    int n;
+    int v[2];
+};
+NcList nc_candidates(int kv, int D) {
+    switch (kv) {
+        case GOLLEK_DTYPE_BF16: return D == 128 ? NcList{2, {8, 7}} : NcList{1, {8, 0}};
+        case GOLLEK_DTYPE_F16: return NcList{1, {8, 0}};
+        case GOLLEK_DTYPE_I8:
+        case GOLLEK_DTYPE_F32: return NcList{2, {11, 8}};
+        default: return NcList{0, {0, 0}};
+    }
+}
+
 // 16-bit KV computes on the tensor pipe; q wider than the MMA type (fp32 q, or any q
-// with f16 KV) is split into hi + lo halves (SPLIT).
-const void *pick_fast(int kv, int D, int G, bool q_f32) {
+// with f16 KV) is split into hi + lo halves (SPLIT).  int8 KV is turned into f16 on the
+// tensor pipe (fp32 q split); fp32 KV runs on packed FFMA.
+const void *pick_fast(int kv, int D, int G, bool q_f32, int nc) {
     switch (kv) {
         case GOLLEK_DTYPE_BF16:
-            if (q_f32)
-                return D == 128 ? pick_g<__nv_bfloat16, 128, true>(G)
-                                : D == 64 ? pick_g<__nv_bfloat16, 64, true>(G) : nullptr;
-            return D == 128 ? pick_g<__nv_bfloat16, 128, false>(G)
-                            : D == 64 ? pick_g<__nv_bfloat16, 64, false>(G) : nullptr;
+            if (D == 128) {
+                if (nc == 8) return q_f32 ? pick_g<__nv_bfloat16, 128, 8, true>(G) : pick_g<__nv_bfloat16, 128, 8, false>(G);
+                if (nc == 7) return q_f32 ? pick_g<__nv_bfloat16, 128, 7, true>(G) : pick_g<__nv_bfloat16, 128, 7, false>(G);
+                return nullptr;
+            }
+            if (D == 64 && nc == 8)
+                return q_f32 ? pick_g<__nv_bfloat16, 64, 8, true>(G) : pick_g<__nv_bfloat16, 64, 8, false>(G);
+            return nullptr;
         case GOLLEK_DTYPE_F16:
-            return D == 128 ? pick_g<__half, 128, true>(G) : D == 64 ? pick_g<__half, 64, true>(G) : nullptr;
+            if (nc != 8) return nullptr;
+            return D == 128 ? pick_g<__half, 128, 8, true>(G) : D == 64 ? pick_g<__half, 64, 8, true>(G) : nullptr;
         case GOLLEK_DTYPE_F32:
-            return D == 128 ? pick_g<float, 128, false>(G) : D == 64 ? pick_g<float, 64, false>(G) : nullptr;
-        case GOLLEK_DTYPE_I8:  // tensor pipe in f16: fp32 q enters as hi + lo
-            if (q_f32) return D == 128 ? pick_g<int8_t, 128, true>(G) : nullptr;
-            return D == 128 ? pick_g<int8_t, 128, false>(G) : nullptr;
+            if (nc == 11) return D == 128 ? pick_g<float, 128, 11, false>(G) : D == 64 ? pick_g<float, 64, 11, false>(G) : nullptr;
+            if (nc == 8) return D == 128 ? pick_g<float, 128, 8, false>(G) : D == 64 ? pick_g<float, 64, 8, false>(G) : nullptr;
+            return nullptr;
+        case GOLLEK_DTYPE_I8:
+            if (D != 128) return nullptr;
+            if (nc == 11) return q_f32 ? pick_g<int8_t, 128, 11, true>(G) : pick_g<int8_t, 128, 11, false>(G);
+            if (nc == 8) return q_f32 ? pick_g<int8_t, 128, 8, true>(G) : pick_g<int8_t, 128, 8, false>(G);
+            return nullptr;
         default:
             return nullptr;
     }
@@ -351,10 +366,12 @@ bool tma_layout_ok(const V2 &p, long long page_stride) {
     return true;
 }
 
-// Eligibility of the mma.sync TMA kernel; returns its function or nullptr.
+// Eligibility of the mma.sync TMA kernel; returns the function of its first compiled
+// warp count or nullptr.
 const void *fast_eligible(const V2 &p, int G, long long page_stride) {
     if (!tma_layout_ok(p, page_stride)) return nullptr;
-    return pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32);
+    const NcList c = nc_candidates(p.kv_dtype, p.D);
+    return c.n ? pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c.v[0]) : nullptr;
 }
 
 // Split-K scratch: the caller's workspace, or the library's per (device, stream) one;
@@ -524,14 +541,30 @@ int run_v2(const V2 &p) {
         const bool quant = p.kv_dtype == GOLLEK_DTYPE_I8;
         const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * kSlabBytes;
         const int max_ctas = sm_count(dev) * 2;
-        const int nc = nc_for(p.kv_dtype);
-        DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, nc, 0, p.S, max_ctas);
-        int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) /
-                                   (2 * tile * nc));
-        spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
-        const int stages = spw * nc;
-        DecodeSmem L = decode_smem_layout(eb, quant, p.D, G, nc, stages, p.S, max_ctas);
-        if (L.total > 227 * 1024) fn = nullptr;
+        // warp count: 16-bit KV takes the candidate with the most stages in flight, int8
+        // and fp32 the first that fits
+        const NcList cand = nc_candidates(p.kv_dtype, p.D);
+        const bool most_stages = eb == 2;
+        int nc = 0, stages = 0;
+        DecodeSmem L{};
+        fn = nullptr;
+        for (int ci = 0; ci < cand.n; ++ci) {
+            const int c = cand.v[ci];
+            const void *f = pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c);
+            if (!f) continue;
+            DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, c, 0, p.S, max_ctas);
+            int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / (2 * tile * c));
+            spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
+            DecodeSmem Lc = decode_smem_layout(eb, quant, p.D, G, c, spw * c, p.S, max_ctas);
+            if (Lc.total > 227 * 1024) continue;
+            if (!fn || (most_stages && spw * c > stages)) {
+                fn = f;
+                nc = c;
+                stages = spw * c;
+                L = Lc;
+                if (!most_stages) break;
+            }
+        }
         if (fn) {
             void *ws = nullptr;
             size_t ws_cap = 0;
