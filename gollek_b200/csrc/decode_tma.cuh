@@ -189,6 +189,7 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quan
     o += NC * kRows * align_up(G, 4) * 4;
     L.comb = o;
     o += NC * G * (D + 2) * 4;
+    o = align_up(o, 16);  // int8 scale slots take 16-byte bulk copies
     L.scales = o;
     o += quant ? stages * 2 * kRows * 4 : 0;
     L.prefix = o;

@@ -557,6 +557,8 @@ int run_v2(const V2 &p) {
             spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
             DecodeSmem Lc = decode_smem_layout(eb, quant, p.D, G, c, spw * c, p.S, max_ctas);
             if (Lc.total > 227 * 1024) continue;
+            // TMA and bulk-copy destinations and vector accesses need these alignments
+            if (Lc.q % 16 || Lc.p % 16 || Lc.scales % 16 || Lc.rstart % 8 || Lc.bars % 8) continue;
             if (!fn || (most_stages && spw * c > stages)) {
                 fn = f;
                 nc = c;
