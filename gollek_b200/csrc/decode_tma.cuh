@@ -10,14 +10,16 @@
 //
 // One CTA = NC consumer warps + 1 producer warp, one CTA per SM.
 //   Producer: works in lane-parallel waves of up to 32 groups, one stage per lane:
-//   each lane reads its group's block-table entries, waits for its stage to be
-//   free and issues 2-D TMA tile loads (SWIZZLE_128B, this CTA only) of the group's K
-//   and V rows, completing on the stage's mbarrier; int8 scales come by 4-byte
-//   cp.async.
+//   each lane reads its group's block-table entries (two waves ahead), polls its
+//   stage's empty mbarrier (non-blocking) and issues TMA tile loads (SWIZZLE_128B, this
+//   CTA only) of the group's K and V rows, completing on the stage's full mbarrier;
+//   int8 scales come by bulk copy, through registers (per page) or by 4-byte cp.async.
+//   (Measured: waves beat per-lane rolling ownership, whose lanes then look up their
+//   next groups one at a time, divergently.)
 //   Consumer warp w owns a ring of SPW stages and takes groups w, w+NC, ... of the
 //   CTA's sequence of groups.  Owning its stages means a warp waits on each stage
 //   barrier in phase order, so parity waits cannot alias.
-//   Score pass: lane l handles token l%16 over head-dim half l/16 against the G
+//   (FFMA consumer, fp32 KV.)  Score pass: lane l handles token l%16 over head-dim half l/16 against the G
 //   query heads of the GQA group (q staged as fp32 in shared memory, broadcast
 //   reads), packed fp32x2 FMAs, halves joined by one shuffle.  Online softmax in the
 //   exp2 domain.  Value pass: lanes 0-15 take even rows and 16-31 odd rows, each lane

@@ -567,3 +567,46 @@ def test_decode_and_append_capture_in_a_cuda_graph(cuda_device):
         g.replay()
         torch.cuda.synchronize()
         assert torch.equal(out, eager)
+
+
+def test_concurrent_callers_on_their_own_streams(cuda_device):
+    """The binding is a process-wide singleton called from many threads: concurrent calls
+    on separate streams (library-owned scratch per stream) and through the legacy
+    synchronous symbol (per-thread stream) all return the oracle's results."""
+    import threading
+
+    from gollek_b200 import ops
+    cases = []
+    for i in range(6):
+        ctx = [300 + 500 * i, 4000 + 700 * i, 33]
+        q, k, v, bt, ctx = decode_case(ctx, hq=8, hkv=8, d=64, bs=16, seed=90 + i)
+        want = oracle_decode(q, k, v, bt, ctx, 0.125, hkv=8, bs=16, lanes=8)
+        a1 = O.a1_execute(q, k, v, bt, ctx, 0.125)
+        cases.append((q, k, v, bt, ctx, want, a1))
+    errors = []
+
+    def worker(i):
+        try:
+            torch.cuda.set_device(cuda_device)
+            q, k, v, bt, ctx, want, a1 = cases[i]
+            dq, dk, dv = _t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device)
+            dbt, dctx = _t(bt, cuda_device), _t(ctx, cuda_device)
+            st = torch.cuda.Stream(cuda_device)
+            for _ in range(5):
+                with torch.cuda.stream(st):
+                    out = ops.paged_attention(dq, dk, dv, dbt, dctx, num_kv_heads=8, block_size=16,
+                                              scale=0.125, num_blocks=k.shape[0], stream=st)
+                st.synchronize()
+                _fp32_close(out.cpu().numpy(), want)
+                leg = torch.empty_like(dq)
+                ops.paged_attention_launch(leg, dq, dk, dv, dbt, dctx, 0.125)
+                _fp32_close(leg.cpu().numpy(), a1)
+        except Exception as e:  # reported below
+            errors.append((i, repr(e)))
+
+    ts = [threading.Thread(target=worker, args=(i,)) for i in range(len(cases))]
+    for t in ts:
+        t.start()
+    for t in ts:
+        t.join()
+    assert not errors, errors
