@@ -535,6 +535,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             // q as A fragments (row g = head g; rows g+8 are zero), split hi + lo when the
             // input is wider than the MMA type so the scores stay fp32-accurate.
             uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
+            float qmul = a.q_scale;  // score multiplier (f16 KV: times the power of two taken out of q)
             if (kQPrefetch && have_qnext) {
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
@@ -543,6 +544,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
             } else {
                 const long long qrow = ((static_cast<long long>(r.s) * Hkv + r.h) * G + g) * D;
+                float qx[KS][2][2];
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
 #pragma unroll
@@ -563,6 +565,30 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                                 x1 = v2.y;
                             }
                         }
+                        qx[kk][hf][0] = x0;
+                        qx[kk][hf][1] = x1;
+                    }
+                }
+                float down = 1.f;
+                if constexpr (std::is_same<KV, __half>::value) {
+                    // keep |q| below the f16 maximum: take a power of two out of q and put it
+                    // back on the scores
+                    float mx = 0.f;
+#pragma unroll
+                    for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf)
+                            mx = fmaxf(mx, fmaxf(fabsf(qx[kk][hf][0]), fabsf(qx[kk][hf][1])));
+                    mx = warp_max(mx);
+                    const int eq = mx >= 16384.f ? min(exp_of(mx) - 14, 126) : 0;
+                    down = pow2i(-eq);
+                    qmul = a.q_scale * pow2i(eq);
+                }
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const float x0 = qx[kk][hf][0] * down, x1 = qx[kk][hf][1] * down;
                         qa[kk][hf] = pack2<KV>(x0, x1);
                         if constexpr (SPLIT) {
                             const float2 back = unpack2<KV>(qa[kk][hf]);
@@ -650,10 +676,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         const int tk = 8 * nt + 2 * t + e;
                         float x2 = s[nt][e];
                         if (a.soft_cap > 0.f) {
-                            x2 *= a.q_scale;
+                            x2 *= qmul;
                             x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
                         } else {
-                            x2 *= a.q_scale;
+                            x2 *= qmul;
                         }
                         x2 = (tk >= v_lo && tk < v_hi) ? x2 : -INFINITY;
                         p[nt][e] = x2;

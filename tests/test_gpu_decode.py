@@ -610,3 +610,32 @@ def test_concurrent_callers_on_their_own_streams(cuda_device):
     for t in ts:
         t.join()
     assert not errors, errors
+
+
+def _round_f16(x):
+    return np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+
+
+@pytest.mark.parametrize("hq,hkv,d,q_f32,qmag", [(32, 8, 128, False, 1.0), (64, 8, 128, True, 1.0),
+                                                 (16, 4, 64, False, 1.0), (32, 8, 128, False, 3e5),
+                                                 (32, 8, 128, True, 3e5)])
+def test_f16_kv_parity(cuda_device, hq, hkv, d, q_f32, qmag):
+    """f16 KV on the tensor pipe (q enters as f16 hi + lo; |q| above the f16 range is
+    brought in by a power of two put back on the scores)."""
+    from gollek_b200 import ops
+    ctx = [1, 70, 900, 4100, 0]
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=d, bs=16, seed=hq + d + int(qmag) % 7, kv_std=0.5)
+    kh, vh = _round_f16(k), _round_f16(v)
+    qq = q * np.float32(qmag)
+    if not q_f32:
+        qq = O.round_bf16(qq)
+    scale = 1.0 / math.sqrt(d)
+    want = oracle_decode(qq, kh, vh, bt, ctx, scale, hkv=hkv, bs=16)
+    out = ops.paged_attention(_t(qq, cuda_device) if q_f32 else _t(qq, cuda_device, torch.bfloat16),
+                              _t(kh, cuda_device, torch.float16), _t(vh, cuda_device, torch.float16),
+                              _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=hkv, block_size=16,
+                              scale=scale, num_blocks=k.shape[0])
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    assert not got[4].any()
