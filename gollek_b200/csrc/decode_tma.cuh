@@ -71,40 +71,12 @@ struct KvType<int8_t> {
     static constexpr bool kQuant = true;
 };
 
-// Decode 4 bytes of KV elements into floats (bf16/f16: 2, f32: 1, int8: 4).
+// Decode 4 bytes of KV elements into floats (the CUDA-core consumer reads fp32 KV).
 template <typename KV>
 __device__ __forceinline__ void decode_word(uint32_t w, float *f);
 template <>
-__device__ __forceinline__ void decode_word<__nv_bfloat16>(uint32_t w, float *f) {
-    f[0] = bf16_lo(w);
-    f[1] = bf16_hi(w);
-}
-template <>
-__device__ __forceinline__ void decode_word<__half>(uint32_t w, float *f) {
-    float2 v = __half22float2(*reinterpret_cast<__half2 *>(&w));
-    f[0] = v.x;
-    f[1] = v.y;
-}
-template <>
 __device__ __forceinline__ void decode_word<float>(uint32_t w, float *f) {
     f[0] = __uint_as_float(w);
-}
-template <>
-__device__ __forceinline__ void decode_word<int8_t>(uint32_t w, float *f) {
-    // Signed byte b -> float: bias to b+128 in [0,255], place it in the low mantissa
-    // byte of 2^23, subtract 2^23 + 128.  Exact.
-    const uint32_t u = w ^ 0x80808080u;
-    const float2 bias = make_float2(-8388736.0f, -8388736.0f);
-    float2 a = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)),
-                           __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)));
-    float2 b = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)),
-                           __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)));
-    a = __fadd2_rn(a, bias);
-    b = __fadd2_rn(b, bias);
-    f[0] = a.x;
-    f[1] = a.y;
-    f[2] = b.x;
-    f[3] = b.y;
 }
 
 // Two floats -> one 32-bit register of the 16-bit MMA type (x0 in the low half).
@@ -492,9 +464,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     // named barrier, so all NC warps take the same barriers.
     const int half = lane >> 4;
     const int li = lane & 15;
-    // int8 scale slot of token li of a stage: per token, or per page (scale_mode 1)
-    const int scale_slot =
-        a.scale_mode == 1 ? li / (a.block_size < kRows ? a.block_size : kRows) : li;
     const uint32_t p_base = smem_u32(sm_p) + warp * kRows * GP * 4;
     volatile int *cons_abort = sm_misc + 3;
 
@@ -1034,6 +1003,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
             }
         } else {
+            // ======== fp32 KV on the CUDA cores (packed FFMA).
+            static_assert(std::is_same<KV, float>::value, "the CUDA-core consumer serves fp32 KV");
             // Stage q (G heads of this kv-head's group), scaled, as fp32.
             {
                 const long long qbase = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
@@ -1105,13 +1076,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         }
                     }
                     const bool valid = li >= v_lo && li < v_hi;
-                    float kscale = 1.f;
-                    if constexpr (QUANT) kscale = sm_scale[stage * 2 * kRows + scale_slot];
     #pragma unroll
                     for (int hh = 0; hh < G; ++hh) {
                         float x2 = dot[hh].x + dot[hh].y;
                         x2 += __shfl_xor_sync(0xffffffffu, x2, 16);
-                        x2 *= kscale;
                         if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
                         sc[hh] = valid ? x2 : -INFINITY;
                     }
@@ -1120,8 +1088,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 // ---------------- online softmax (exp2 domain), per head over the 16 tokens
                 bool rescale = false;
                 float alpha[G], pw[GP];
-                float vscale = 1.f;
-                if constexpr (QUANT) vscale = sm_scale[stage * 2 * kRows + kRows + scale_slot];
     #pragma unroll
                 for (int hh = 0; hh < G; ++hh) {
                     float mx = sc[hh];
@@ -1134,7 +1100,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     const float mref = (mn == -INFINITY) ? 0.f : mn;
                     const float p = fast_exp2(sc[hh] - mref);
                     l[hh] = l[hh] * alpha[hh] + (half == 0 ? p : 0.f);
-                    pw[hh] = p * vscale;
+                    pw[hh] = p;
                 }
     #pragma unroll
                 for (int hh = G; hh < GP; ++hh) pw[hh] = 0.f;
