@@ -499,10 +499,7 @@ def bench_decode(args, world, rank, local):
             .get(args.workload, "bf16 KV/q/out, f32 accumulate"),
             "data": "synthetic (seeded; BASELINE shapes and distributions)",
             "config": {
-                "workload": {"decode_bf16": "config2_llama3_8b_bf16_gqa_decode",
-                             "decode_int8": "config3_int8_kv_decode",
-                             "decode_fp32": "fp32_gqa_decode",
-                             "longctx": "config5_llama3_70b_longctx_kvhead_sharded"}[args.workload],
+                "workload": WORKLOAD_NAMES[args.workload],
                 "batch_per_gpu": B if args.workload != "longctx" else B,
                 "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"], "head_dim": sh["d"],
                 "block_size": sh["bs"], "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
@@ -763,15 +760,25 @@ def bench_reference(args):
         "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": r["seconds_per_step"] * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "scaling": "strong" if args.workload == "longctx" else "weak", "vs_baseline": None,
         "dtype": "f32 (reference CPU path)", "data": "synthetic (seeded; same shapes as ours)",
-        "config": {"workload": args.workload, "batch": B, "num_q_heads": hq, "num_kv_heads": hkv,
-                   "head_dim": D, "block_size": BS},
+        "config": {"workload": WORKLOAD_NAMES[args.workload], "batch_per_gpu": B, "num_q_heads": sh["hq"],
+                   "num_kv_heads": sh["hkv"], "head_dim": D, "block_size": BS,
+                   "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
+                   "context_tokens_per_gpu": int(ctx.sum()), "kv_heads_per_gpu": hkv,
+                   "parallelism": (f"kv-head shard x{world}" if args.workload == "longctx"
+                                   else f"independent batches x{world}")},
         "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"],
                          "kind": r["kind"], "sample": r["sample"]},
         "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+WORKLOAD_NAMES = {"decode_bf16": "config2_llama3_8b_bf16_gqa_decode",
+                  "decode_int8": "config3_int8_kv_decode",
+                  "decode_fp32": "fp32_gqa_decode",
+                  "longctx": "config5_llama3_70b_longctx_kvhead_sharded"}
 
 
 def main():
