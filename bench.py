@@ -42,7 +42,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode_bf16",
-                    choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate"])
+                    choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate", "config1"])
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--gather", action="store_true", help="longctx: all-gather head-sharded outputs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -662,6 +662,119 @@ def bench_migrate(args, world, rank, local):
         }), flush=True)
 
 
+def config1_case(seed):
+    """fp32 MHA decode, 4 sequences of {37, 128, 301, 512} tokens, 8 heads,
+    head_dim 64, block 16, a seeded permutation of a 256-block pool, N(0, 1) values, scale 1/8."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    ctx = np.array([37, 128, 301, 512], np.int32)
+    perm = rng.permutation(256).astype(np.int32)
+    bt = np.zeros((4, 32), np.int32)
+    off = 0
+    for s, c in enumerate(ctx):
+        n = (int(c) + 15) // 16
+        bt[s, :n] = perm[off:off + n]
+        off += n
+    q = rng.standard_normal((4, 8, 64)).astype(np.float32)
+    k = rng.standard_normal((256, 8, 16, 64)).astype(np.float32)
+    v = rng.standard_normal((256, 8, 16, 64)).astype(np.float32)
+    alg = int(ctx.sum()) * 8 * 64 * 4 * 2 + q.nbytes * 2 + bt.size * 4 + ctx.nbytes
+    return q, k, v, bt, ctx, 0.125, alg
+
+
+def cpu_config1_baseline(seed, seconds=10.0):
+    """PagedAttentionCpuFallback.execute (the reference's fp32 CPU path, single-threaded as
+    in Java) restated in oracle/oracle.c, on config 1."""
+    from oracle import oracle as O
+    q, k, v, bt, ctx, scale, _ = config1_case(seed)
+    O.a1_execute(q, k, v, bt, ctx, scale)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        O.a1_execute(q, k, v, bt, ctx, scale)
+        reps += 1
+    el = time.perf_counter() - t0
+    return {"value": 4 * reps / el, "unit": "tokens/s", "cores": 1, "kind": "port",
+            "seconds_per_step": el / reps,
+            "sample": f"the whole config 1 batch, {reps} repetitions in {el:.1f} s; oracle/oracle.c "
+                      "oracle_a1_execute (PagedAttentionCpuFallback restatement), one thread"}
+
+
+def bench_config1(args, world, rank, local):
+    """BASELINE config 1 through the legacy synchronous symbol paged_attention_launch (the
+    reference's FFM entry point): latency-bound at 4 sequences, reported as tokens/s with
+    the GB/s of its 4 MB step."""
+    import torch
+    from gollek_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    q, k, v, bt, ctx, scale, alg = config1_case(args.seed)
+    dq, dk, dv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    dbt, dctx = torch.from_numpy(bt).to(dev), torch.from_numpy(ctx).to(dev)
+    out = torch.empty_like(dq)
+    per_thread = torch.cuda.ExternalStream(2, device=dev)  # cudaStreamPerThread, the symbol's stream
+
+    def step():
+        ops.paged_attention_launch(out, dq, dk, dv, dbt, dctx, scale)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(per_thread)
+        for _ in range(args.steps):
+            step()
+        e1.record(per_thread)
+        torch.cuda.synchronize()
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    # e2e: pinned host q, tables, lengths -> H2D -> the legacy call -> D2H of out
+    hq, hbt, hctx = (torch.from_numpy(x).pin_memory() for x in (q, bt, ctx))
+    hout = torch.empty_like(out, device="cpu").pin_memory()
+    e2e_steps = max(1, min(args.steps, 200))
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(per_thread)
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(per_thread):
+            dq.copy_(hq, non_blocking=True)
+            dbt.copy_(hbt, non_blocking=True)
+            dctx.copy_(hctx, non_blocking=True)
+        step()
+        with torch.cuda.stream(per_thread):
+            hout.copy_(out, non_blocking=True)
+    f1.record(per_thread)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    if rank != 0:
+        return
+    per_s = t_ms / 1e3 / args.steps
+    gbs = alg / per_s / 1e9
+    peak, peak_kind = peaks()
+    cpu = None if args.no_cpu_baseline or world > 1 else cpu_config1_baseline(args.seed)
+    if cpu:
+        cpu.pop("seconds_per_step", None)
+    print(json.dumps({
+        "metric": METRIC, "value": 4 * world / per_s, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE config 1)",
+        "config": {"workload": "config1_fp32_mha_decode_legacy_symbol", "batch_per_gpu": 4,
+                   "num_heads": 8, "head_dim": 64, "block_size": 16, "context": "{37,128,301,512}",
+                   "pool_blocks": 256, "entry_point": "paged_attention_launch (synchronous)",
+                   "l2": "4 MB step: L2-resident after the first call (latency-bound size)"},
+        "hbm_gbs": gbs,
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "traffic": None, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                     "algorithmic_bytes_per_launch": alg, "kernel": "decode_tma_kernel<float,64,1,...>",
+                     "note": "latency-bound: 4 sequences, each call synchronises its stream"},
+        "e2e": {"value": 4 * world * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": q.nbytes + bt.nbytes + ctx.nbytes, "d2h_bytes_per_step": q.nbytes,
+                "steps": e2e_steps,
+                "path": "pinned host q/tables/lengths -> H2D -> paged_attention_launch -> D2H out"},
+        "gpu_launches": args.steps, "clocks": clk.summary(), "cpu_baseline": cpu,
+    }), flush=True)
+
+
 def cpu_migrate_baseline(seed, seconds=3.0, sample_blocks=128):
     """The reference's migration loop (transferKvToDecodePartition: per (block, layer)
     copyFrom of 32 KiB slices, PD/PrefillDecodeDisaggService.java:415-429) restated in
@@ -702,6 +815,19 @@ def bench_reference(args):
         return
     import numpy as np
     from oracle import oracle as O
+    if args.workload == "config1":
+        r = cpu_config1_baseline(args.seed, seconds=max(1.0, min(20.0, 0.5 * args.steps)))
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["seconds_per_step"] * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (reference CPU path)", "data": "synthetic (seeded; BASELINE config 1)",
+            "config": {"workload": "config1_fp32_mha_decode_legacy_symbol", "batch_per_gpu": 4,
+                       "num_heads": 8, "head_dim": 64, "block_size": 16, "context": "{37,128,301,512}"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
     if args.workload == "migrate":
         r = cpu_migrate_baseline(args.seed, seconds=max(1.0, min(20.0, 2.0 * args.steps)))
         print(json.dumps({
@@ -790,6 +916,8 @@ def main():
     try:
         if args.workload == "migrate":
             bench_migrate(args, world, rank, local)
+        elif args.workload == "config1":
+            bench_config1(args, world, rank, local)
         else:
             bench_decode(args, world, rank, local)
     finally:
