@@ -1,24 +1,27 @@
 // decode_common.cuh -- what the persistent decode kernels share: the argument block,
-// the 16-token group as the unit of work, and the stream-K schedule that cuts the
-// groups of all (sequence, kv-head) pairs into one contiguous range per CTA.
+// the token group (16 tokens; 32 in the int8 kernel) as the unit of work, and the
+// stream-K schedule that cuts the groups of all (sequence, kv-head) pairs into one
+// contiguous range per CTA.
 //
 // Linear group space: unit x = prefix[s] * Hkv + h * n_s + g, where n_s is the number
-// of 16-token groups in sequence s's attention window and g the group within it.  CTA
-// ranges are cut in cost space, where each (sequence, kv-head) costs its groups plus
-// kRunCost, so a CTA that starts many runs gets fewer groups.  A range covers runs of
-// consecutive groups of one (sequence, kv-head); a run that does not cover its whole
-// (sequence, kv-head) is a split-K piece, merged by the CTA that finishes last.
+// of groups in sequence s's attention window and g the group within it.  CTA ranges
+// are cut in cost space, where each (sequence, kv-head) costs its groups plus a run
+// cost (kRunCost 16-token groups), so a CTA that starts many runs gets fewer groups.
+// A range covers runs of consecutive groups of one (sequence, kv-head); a run that does
+// not cover its whole (sequence, kv-head) is a split-K piece, merged by the CTA that
+// finishes last.
 #pragma once
 
 #include "common.cuh"
 
 namespace gk {
 
-constexpr int kRows = 16;          // tokens per group
+constexpr int kRows = 16;          // tokens per group (DecodeArgs::group_rows may be 32)
 constexpr int kSlabBytes = kRows * 128;
 constexpr int kMaxSplits = 64;     // split-K pieces per (sequence, kv-head) at most
 constexpr int kMaxFastSeqs = 16384;
 constexpr int kMinRunGroups = 8;   // smallest per-CTA range, in groups
+constexpr int kMaxStagesPerWarp = 6;  // stage ring of one consumer warp, at most
 // Cost of starting a run (a q load, a merge of the warp states, maybe a split-K
 // exchange), in 16-token groups; CTAs are balanced on groups + kRunCost per run.
 #ifndef GK_RUN_COST
@@ -44,6 +47,7 @@ struct DecodeArgs {
     int num_vstages;      // tensor-memory kernel: V tiles
     int box3d;            // 1: one 3-D TMA box (all 128-byte slabs of 16 rows) per page
     int seq_div;          // block-table row of sequence s is s / seq_div (queries of one sequence)
+    int group_rows;       // tokens per group: 16, or 32 (int8 kernel with 32-token stages)
     int scale_mode;       // int8: 0 per-token scales by bulk copy, 1 one scale per page, 2 general
     float q_scale;        // applied to q when staged: scale*log2(e), or scale with soft-cap
     float soft_cap;       // > 0: cap*tanh(score/cap)
@@ -60,7 +64,8 @@ __device__ __forceinline__ void store_out(void *out, long long idx, float v, int
         reinterpret_cast<float *>(out)[idx] = v;
 }
 
-// Window of one sequence: groups [g_lo, g_lo + n) of 16 tokens cover [win_start, len).
+// Window of one sequence: groups [g_lo, g_lo + n) of group_rows tokens cover
+// [win_start, len).
 struct SeqWin {
     int len, win_start, g_lo, n;
 };
@@ -72,8 +77,9 @@ __device__ __forceinline__ SeqWin seq_win(const DecodeArgs &a, int s) {
     len = len < 0 ? 0 : (len > cap ? cap : len);
     w.len = len;
     w.win_start = (a.window > 0 && len > a.window) ? len - a.window : 0;
-    w.g_lo = w.win_start / kRows;
-    w.n = len > 0 ? (len + kRows - 1) / kRows - w.g_lo : 0;
+    const int gr = a.group_rows;
+    w.g_lo = w.win_start / gr;
+    w.n = len > 0 ? (len + gr - 1) / gr - w.g_lo : 0;
     return w;
 }
 
@@ -147,6 +153,7 @@ __device__ inline Schedule schedule_prologue(const DecodeArgs &a, int *sm_prefix
     const int lane = tid & 31;
     const int S = a.num_seqs;
     const int Hkv = a.num_kv_heads;
+    const int run_cost = kRunCost * kRows / a.group_rows;  // in this launch's groups
     // Exclusive prefix of per-sequence group counts (contiguous segment per thread).
     {
         const int seg = (S + NT - 1) / NT;
@@ -160,9 +167,9 @@ __device__ inline Schedule schedule_prologue(const DecodeArgs &a, int *sm_prefix
             sm_len[s] = w0.len;
             const int n = w0.n;
             sm_prefix[s] = n;
-            sm_cprefix[s] = n > 0 ? n + kRunCost : 0;
+            sm_cprefix[s] = n > 0 ? n + run_cost : 0;
             sum += n;
-            csum += n > 0 ? n + kRunCost : 0;
+            csum += n > 0 ? n + run_cost : 0;
             mx = max(mx, n);
         }
         int incl = sum, cincl = csum;
@@ -234,12 +241,12 @@ __device__ inline Schedule schedule_prologue(const DecodeArgs &a, int *sm_prefix
                 hi = mid - 1;
         }
         const int n = sm_prefix[lo + 1] - sm_prefix[lo];
-        const int m = n + kRunCost;
+        const int m = n + run_cost;
         const int y = static_cast<int>(c - static_cast<long long>(sm_cprefix[lo]) * Hkv);
         const int h = y / m;
         const int v = y - h * m;
         return static_cast<long long>(sm_prefix[lo]) * Hkv + static_cast<long long>(h) * n +
-               (v > kRunCost ? v - kRunCost : 0);
+               (v > run_cost ? v - run_cost : 0);
     };
     for (int b = tid; b <= static_cast<int>(gridDim.x); b += NT)
         sm_rstart[b] = b >= sch.g_eff ? sch.total : x_of_cost(static_cast<long long>(b) * per_cost);

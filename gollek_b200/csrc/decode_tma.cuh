@@ -1,10 +1,12 @@
 // decode_tma.cuh -- persistent, warp-specialised paged decode attention for sm_100a.
 //
-// Work: the unit is a 16-token group of one (sequence, kv-head).  The prologue of
-// every CTA derives, from the context lengths, the linear order of all groups
-// (sequence-major, then kv-head, then position) and cuts it into gridDim.x equal
-// contiguous ranges (stream-K style): every CTA moves the same number of KV bytes,
-// whatever the length mix.  A range covers runs of consecutive groups of one
+// Work: the unit is a group of ROWS tokens of one (sequence, kv-head): 16, or 32 for
+// int8 KV with bf16 q and pages of >= 16 tokens (a stage then carries as many bytes as
+// a 16-bit one and the per-group costs are paid half as often).  The prologue of every
+// CTA derives, from the context lengths, the linear order of all groups
+// (sequence-major, then kv-head, then position) and cuts it into gridDim.x contiguous
+// ranges of equal cost (stream-K style): every CTA moves about the same number of KV
+// bytes, whatever the length mix.  A range covers runs of consecutive groups of one
 // (sequence, kv-head); a run that does not cover its whole (sequence, kv-head) is a
 // split-K piece.
 //
@@ -29,7 +31,7 @@
 //   and the CTA completing the last piece merges all of them (log-sum-exp) and
 //   resets the arrival counter, so the scratch stays zeroed between calls.
 //
-// Stage layout: 128-byte-wide column slabs of 16 rows (2 KB); 16-byte chunk c of
+// Stage layout: 128-byte-wide column slabs of ROWS rows; 16-byte chunk c of
 // row r sits at chunk position c ^ (r & 7), which is what TMA's 128-byte swizzle
 // writes.  The 8 lanes of a quarter-warp read 8 rows of one logical chunk, or 8
 // chunks of one row: 8 distinct bank groups either way.
@@ -132,9 +134,10 @@ __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) 
 // Unbiased exponent of a positive finite float (x in [2^e, 2^(e+1))); normals only.
 __device__ __forceinline__ int exp_of(float x) { return static_cast<int>((__float_as_uint(x) >> 23) & 0xffu) - 127; }
 
-// Byte offset in a swizzled stage tile of byte `b` of row `r`.
+// Byte offset in a swizzled stage tile (slabs of ROWS rows) of byte `b` of row `r`.
+template <int ROWS = kRows>
 __device__ __forceinline__ uint32_t swz(int r, int b) {
-    return static_cast<uint32_t>((b >> 7) * kSlabBytes + r * 128 +
+    return static_cast<uint32_t>((b >> 7) * (ROWS * 128) + r * 128 +
                                  ((((b >> 4) & 7) ^ (r & 7)) << 4) + (b & 15));
 }
 
@@ -151,21 +154,21 @@ struct DecodeSmem {
 
 __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quant, int D, int G,
                                                          int NC, int stages, int num_seqs,
-                                                         int num_ctas) {
+                                                         int num_ctas, int rows) {
     DecodeSmem L;
-    const uint32_t tile = static_cast<uint32_t>(D * kv_bytes / 128) * kSlabBytes;
+    const uint32_t tile = static_cast<uint32_t>(D * kv_bytes / 128) * rows * 128;
     uint32_t o = 0;
     L.stages = o;
     o += stages * 2 * tile;
     L.q = o;
     o += align_up(G * (D + 4 * (D / 64)) * 4, 16);
     L.p = o;
-    o += NC * kRows * align_up(G, 4) * 4;
+    o += NC * rows * align_up(G, 4) * 4;
     L.comb = o;
     o += NC * G * (D + 2) * 4;
     o = align_up(o, 16);  // int8 scale slots take 16-byte bulk copies
     L.scales = o;
-    o += quant ? stages * 2 * kRows * 4 : 0;
+    o += quant ? stages * 2 * rows * 4 : 0;
     L.prefix = o;
     o += (num_seqs + 1) * 4;
     L.cprefix = o;
@@ -183,9 +186,10 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quan
     return L;
 }
 
-// SPLIT (16-bit KV only): q is wider than the MMA type (fp32 q, or any q with f16 KV)
-// and enters the score MMA as hi + lo halves.
-template <typename KV, int D, int G, int NC, bool SPLIT>
+// SPLIT (tensor-pipe consumers): q is wider than the MMA type (fp32 q, or any q with
+// f16 KV or int8 KV) and enters the score MMA as hi + lo halves.  ROWS: tokens per
+// group and stage (32 only for int8 KV; the launch sets DecodeArgs::group_rows to it).
+template <typename KV, int D, int G, int NC, bool SPLIT, int ROWS = kRows>
 __global__ void __launch_bounds__((NC + 1) * 32, 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
@@ -194,7 +198,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     constexpr bool I8MMA = std::is_same<KV, int8_t>::value && D == 128;  // int8 on the tensor pipe
     constexpr int ROW_BYTES = D * KB;
     constexpr int NSLAB = ROW_BYTES / 128;
-    constexpr int TILE = NSLAB * kSlabBytes;
+    constexpr int SLAB = ROWS * 128;         // bytes of one 128-byte column slab
+    constexpr int TILE = NSLAB * SLAB;
     constexpr int HALF_CH = ROW_BYTES / 32;  // 16-byte chunks per head-dim half
     constexpr int EPC = 16 / KB;             // elements per chunk
     constexpr int EPW = 4 / KB;              // elements per 32-bit word
@@ -206,13 +211,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     static_assert(ROW_BYTES % 128 == 0, "row must be a whole number of 128-byte slabs");
     static_assert(EPL % 2 == 0 && EPC % 4 == 0 && D % 64 == 0, "vector widths");
     static_assert(NSLAB * 2 * 2 <= 32, "TMA loads of one stage (<= 2 pages) fit a warp");
+    static_assert(ROWS == kRows || (I8MMA && ROWS == 32), "32-token groups: int8 KV only");
 
     extern __shared__ __align__(16) uint8_t smem_raw[];
     // Align to 1024 bytes by pointer arithmetic on the shared array (keeps the
     // shared address space visible to the compiler).
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const DecodeSmem L =
-        decode_smem_layout(KB, QUANT, D, G, NC, a.num_stages, a.num_seqs, gridDim.x);
+        decode_smem_layout(KB, QUANT, D, G, NC, a.num_stages, a.num_seqs, gridDim.x, ROWS);
     uint8_t *sm_stage = smem + L.stages;
     float *sm_q = reinterpret_cast<float *>(smem + L.q);
     float *sm_p = reinterpret_cast<float *>(smem + L.p);
@@ -267,8 +273,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         // stage to be free and issues its own TMA loads, without waiting for the other
         // lanes.  The next wave's page ids are looked up (block-table loads in flight)
         // while the current wave waits and issues, so a wave starts with its ids ready.
-        const int R = a.block_size < kRows ? a.block_size : kRows;  // rows per TMA box
-        const int npg = kRows / R;                                  // pages per stage (<= 2)
+        const int R = a.block_size < ROWS ? a.block_size : ROWS;  // rows per TMA box
+        const int npg = ROWS / R;                                 // pages per stage (<= 2)
         const int W = NS < GK_WAVE ? NS : GK_WAVE;  // groups per producer wave
         struct GroupLoc {
             int h, t0, row_off, pid0, pid1, stage, round, len, win_start;
@@ -284,9 +290,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             q.h = r.h;
             q.stage = stage_of(gi);
             q.round = round_of(gi);
-            q.t0 = (q.win_start / kRows + r.g) * kRows;
+            q.t0 = (q.win_start / ROWS + r.g) * ROWS;
             const int p_first = q.t0 / a.block_size;
-            q.row_off = a.block_size < kRows ? 0 : q.t0 % a.block_size;
+            q.row_off = a.block_size < ROWS ? 0 : q.t0 % a.block_size;
             const int pages_in_seq = (len + a.block_size - 1) / a.block_size;
             const int *bt = a.block_tables + static_cast<long long>(r.s / a.seq_div) * a.max_blocks;
             q.pid0 = q.pid1 = 0;
@@ -337,12 +343,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             uint8_t *vdst = kdst + TILE;
             if constexpr (QUANT) {
                 if (page_scales) {
-                    float *ks = sm_scale + stage * 2 * kRows;
+                    float *ks = sm_scale + stage * 2 * ROWS;
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         if (j >= npg || !((loaded >> j) & 1)) continue;
                         ks[j] = q.ks[j];
-                        ks[kRows + j] = q.vs[j];
+                        ks[ROWS + j] = q.vs[j];
                     }
                 }
             }
@@ -353,21 +359,21 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (!((loaded >> j) & 1)) continue;
                 const long long y = static_cast<long long>(j ? pid1 : pid0) * a.page_rows +
                                     static_cast<long long>(q.h) * a.block_size + q.row_off;
-                if (a.box3d) {  // 16 rows x all slabs in one box each for K and V
+                if (a.box3d) {  // ROWS rows x all slabs in one box each for K and V
                     tma_load_3d(kdst, &tm_k, 0, static_cast<int>(y), 0, &full_bar[stage]);
                     tma_load_3d(vdst, &tm_v, 0, static_cast<int>(y), 0, &full_bar[stage]);
                     continue;
                 }
 #pragma unroll
                 for (int slab = 0; slab < NSLAB; ++slab) {
-                    tma_load_2d(kdst + slab * kSlabBytes + j * R * 128, &tm_k, slab * (128 / KB),
+                    tma_load_2d(kdst + slab * SLAB + j * R * 128, &tm_k, slab * (128 / KB),
                                 static_cast<int>(y), &full_bar[stage]);
-                    tma_load_2d(vdst + slab * kSlabBytes + j * R * 128, &tm_v, slab * (128 / KB),
+                    tma_load_2d(vdst + slab * SLAB + j * R * 128, &tm_v, slab * (128 / KB),
                                 static_cast<int>(y), &full_bar[stage]);
                 }
             }
             if constexpr (QUANT) {
-                float *ks = sm_scale + stage * 2 * kRows;
+                float *ks = sm_scale + stage * 2 * ROWS;
                 if (a.scale_mode == 0) {
                     // per-token scales: R contiguous floats per page, one bulk copy each
                     for (int j = 0; j < npg; ++j) {
@@ -375,10 +381,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         const long long so = static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
                                              static_cast<long long>(q.h) * a.scale_head_stride + q.row_off;
                         bulk_load(ks + j * R, a.k_scales + so, R * 4u, &full_bar[stage]);
-                        bulk_load(ks + kRows + j * R, a.v_scales + so, R * 4u, &full_bar[stage]);
+                        bulk_load(ks + ROWS + j * R, a.v_scales + so, R * 4u, &full_bar[stage]);
                     }
                 } else if (a.scale_mode == 2) {
-                    for (int tk = 0; tk < kRows; ++tk) {
+                    for (int tk = 0; tk < ROWS; ++tk) {
                         const int t = q.t0 + tk;
                         const int j = tk / R;
                         if (t >= q.win_start && t < q.len && ((loaded >> j) & 1)) {
@@ -386,7 +392,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                                                  static_cast<long long>(q.h) * a.scale_head_stride +
                                                  static_cast<long long>(t % a.block_size) * a.scale_token_stride;
                             cp_async_4(ks + tk, a.k_scales + so);
-                            cp_async_4(ks + kRows + tk, a.v_scales + so);
+                            cp_async_4(ks + ROWS + tk, a.v_scales + so);
                         }
                     }
                     cp_async_mbar_arrive_noinc(&full_bar[stage]);
@@ -464,7 +470,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     // named barrier, so all NC warps take the same barriers.
     const int half = lane >> 4;
     const int li = lane & 15;
-    const uint32_t p_base = smem_u32(sm_p) + warp * kRows * GP * 4;
+    const uint32_t p_base = smem_u32(sm_p) + warp * ROWS * GP * 4;
     volatile int *cons_abort = sm_misc + 3;
 
     // Sequences with nothing to attend to: zeros, written by CTA s % grid.
@@ -489,7 +495,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         SeqWin sw;
         sw.len = sm_len[r.s];
         sw.win_start = (a.window > 0 && sw.len > a.window) ? sw.len - a.window : 0;
-        sw.g_lo = sw.win_start / kRows;
+        sw.g_lo = sw.win_start / ROWS;
         sw.n = sm_prefix[r.s + 1] - sm_prefix[r.s];
 
         if constexpr (KB == 2) {
@@ -498,6 +504,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             // 16); values O^T = V^T P^T with head_dim as rows, the heads as the 8
             // columns, so the probabilities go from the score accumulators straight
             // into the B operand.
+            static_assert(ROWS == 16, "16-bit consumer: 16-token groups");
             constexpr int KS = D / 16;  // k-steps of the score MMA = m-tiles of the value MMA
             const int g = lane >> 2;    // fragment row group
             const int t = lane & 3;     // fragment column pair
@@ -737,11 +744,16 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             // K word is one B fragment pair, and q is loaded in the same order.  Value rows
             // (head_dim) likewise: lane row group g owns dims [16g, 16g+16); m-tile mt row
             // g is dim 16g+2mt and row g+8 is dim 16g+2mt+1.
+            // A group of ROWS tokens is NT score n-tiles of 8 tokens and VK value k-steps
+            // of 16 tokens; 16-token groups keep two accumulator chains per n-tile.
             constexpr int KS = D / 16;
+            constexpr int NT = ROWS / 8;
+            constexpr int VK = ROWS / 16;
+            constexpr int CH = NT >= 4 ? 1 : 2;
             static_assert(D == 128, "int8 tensor-pipe path: head_dim 128");
             const int g = lane >> 2;
             const int t = lane & 3;
-            const int R = a.block_size < kRows ? a.block_size : kRows;
+            const int R = a.block_size < ROWS ? a.block_size : ROWS;
             uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
             float qmul;         // score multiplier: q_scale times the power of two taken out of q
             float qsum = 0.f;   // head g's sum of the f16 q values the MMAs see
@@ -833,57 +845,54 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
                 const uint32_t kt = smem_u32(sm_stage) + static_cast<uint32_t>(stage) * 2 * TILE;
                 const uint32_t vt = kt + TILE;
-                const int t0 = (sw.g_lo + r.g + j) * kRows;
+                const int t0 = (sw.g_lo + r.g + j) * ROWS;
                 const int v_lo = max(sw.win_start - t0, 0);
-                const int v_hi = min(sw.len - t0, kRows);
-                // ---------------- raw K and V words and the scales to registers, then free
-                // the stage (int8 rows outside the window are finite integers: no clearing)
-                uint4 kr[2][2], vr[4];
+                const int v_hi = min(sw.len - t0, ROWS);
+                // ---------------- raw K words and the scales to registers (int8 rows outside
+                // the window are finite integers: no clearing); the V words follow the score
+                // MMAs, so K and V words are never live together
+                uint4 kr[NT][2];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) kr[nt][hf] = lds_u4(kt + swz(g + 8 * nt, 32 * t + 16 * hf));
+                    for (int hf = 0; hf < 2; ++hf)
+                        kr[nt][hf] = lds_u4(kt + swz<ROWS>(g + 8 * nt, 32 * t + 16 * hf));
+                const uint32_t sc = smem_u32(sm_scale) + static_cast<uint32_t>(stage) * 2 * ROWS * 4;
+                // scales of tokens 8nt + 2t + e: one per page (slot = token / R), or per token
+                auto read_scales = [&](float (*dst)[2], uint32_t base) {
+                    if (a.scale_mode == 1) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) vr[i] = lds_u4(vt + swz(2 * t + (i & 1) + 8 * (i >> 1), 16 * g));
-                float ksc[2][2], vsc[2][2];
-                {
-                    const uint32_t sc = smem_u32(sm_scale) + static_cast<uint32_t>(stage) * 2 * kRows * 4;
-                    if (a.scale_mode == 1) {  // one scale per page (slot = token / R)
-#pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            const int slot = (8 * nt) / R;
-                            const uint32_t k1 = sc + static_cast<uint32_t>(slot) * 4;
-                            float kf, vf;
-                            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(kf) : "r"(k1));
-                            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(vf) : "r"(k1 + kRows * 4));
-                            ksc[nt][0] = ksc[nt][1] = kf;
-                            vsc[nt][0] = vsc[nt][1] = vf;
+                        for (int nt = 0; nt < NT; ++nt) {
+                            float f;
+                            asm volatile("ld.shared.f32 %0, [%1];"
+                                         : "=f"(f)
+                                         : "r"(base + static_cast<uint32_t>((8 * nt) / R) * 4));
+                            dst[nt][0] = dst[nt][1] = f;
                         }
-                    } else {  // per token: tokens 2t, 2t+1 of each n-tile are adjacent
+                    } else {  // tokens 2t, 2t+1 of each n-tile are adjacent
 #pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            const uint2 kw = lds_u2(sc + (8 * nt + 2 * t) * 4);
-                            const uint2 vw = lds_u2(sc + (kRows + 8 * nt + 2 * t) * 4);
-                            ksc[nt][0] = __uint_as_float(kw.x);
-                            ksc[nt][1] = __uint_as_float(kw.y);
-                            vsc[nt][0] = __uint_as_float(vw.x);
-                            vsc[nt][1] = __uint_as_float(vw.y);
+                        for (int nt = 0; nt < NT; ++nt) {
+                            const uint2 w2 = lds_u2(base + (8 * nt + 2 * t) * 4);
+                            dst[nt][0] = __uint_as_float(w2.x);
+                            dst[nt][1] = __uint_as_float(w2.y);
                         }
                     }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty_bar[stage]);
+                };
+                float ksc[NT][2], vsc[NT][2];
+                read_scales(ksc, sc);
                 // ---------------- scores
-                float s[2][4], s2[2][4];
+                float s[CH][NT][4];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                for (int c = 0; c < CH; ++c)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) s[nt][e] = s2[nt][e] = 0.f;
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) s[c][nt][e] = 0.f;
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
-                    float(*acc)[4] = (kk & 1) ? s2 : s;
+                    float(*acc)[4] = s[kk % CH];
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
+                    for (int nt = 0; nt < NT; ++nt) {
                         const uint4 &q4 = kr[nt][kk >> 2];
                         const uint32_t w = (kk & 3) == 0 ? q4.x : (kk & 3) == 1 ? q4.y : (kk & 3) == 2 ? q4.z : q4.w;
                         uint32_t b0, b1;
@@ -892,22 +901,38 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         if constexpr (SPLIT) mma_16816<__half>(acc[nt], ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
                     }
                 }
+                // ---------------- V words and scales to registers, then free the stage
+                uint4 vr[VK][4];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                for (int vk = 0; vk < VK; ++vk)
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) s[nt][e] = (s[nt][e] + s2[nt][e]) - qbias;
+                    for (int i = 0; i < 4; ++i)
+                        vr[vk][i] = lds_u4(vt + swz<ROWS>(16 * vk + 2 * t + (i & 1) + 8 * (i >> 1), 16 * g));
+                read_scales(vsc, sc + ROWS * 4);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty_bar[stage]);
+                if constexpr (CH == 2) {
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) s[0][nt][e] += s[1][nt][e];
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) s[0][nt][e] -= qbias;
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
-                float p[2][2];
-                bool valid[2][2];
+                float p[NT][2];
+                bool valid[NT][2];
                 float mloc = -INFINITY;
                 float vmax = 0.f;
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int tk = 8 * nt + 2 * t + e;
                         valid[nt][e] = tk >= v_lo && tk < v_hi;
-                        float x2 = s[nt][e] * qmul * ksc[nt][e];
+                        float x2 = s[0][nt][e] * qmul * ksc[nt][e];
                         if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
                         x2 = valid[nt][e] ? x2 : -INFINITY;
                         p[nt][e] = x2;
@@ -930,9 +955,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
                 const float vmul = pow2i(-ev_new);
                 float psum = 0.f;
-                float pv[2][2];
+                float pv[NT][2];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const float pe = fast_exp2(p[nt][e] - mref);
@@ -940,11 +965,18 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         pv[nt][e] = valid[nt][e] ? pe * (vsc[nt][e] * vmul) : 0.f;
                     }
                 l_run = l_run * alpha + psum;
-                const uint32_t pb0 = pack2<__half>(pv[0][0], pv[0][1]);
-                const uint32_t pb1 = pack2<__half>(pv[1][0], pv[1][1]);
-                const float2 pr0 = unpack2<__half>(pb0), pr1 = unpack2<__half>(pb1);
+                // probabilities as the value MMA's B fragments: n-tile nt holds tokens
+                // 8nt + 2t, 8nt + 2t + 1 of head g, i.e. k rows 2t, 2t+1 (+8) of k-step nt / 2
+                uint32_t pb[NT];
+                float pmass = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    pb[nt] = pack2<__half>(pv[nt][0], pv[nt][1]);
+                    const float2 pr = unpack2<__half>(pb[nt]);
+                    pmass += pr.x + pr.y;
+                }
                 const float fac = ev_set ? alpha * pow2i(max(-126, min(127, ev - ev_new))) : alpha;
-                ps_run = ps_run * fac + ((pr0.x + pr0.y) + (pr1.x + pr1.y));
+                ps_run = ps_run * fac + pmass;
                 ev = ev_new;
                 ev_set = true;
                 if (__any_sync(0xffffffffu, fac != 1.f)) {
@@ -958,20 +990,24 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         o[mt][3] *= al1;
                     }
                 }
-                // ---------------- values: rows 2t, 2t+1 (a0, a1) and 2t+8, 2t+9 (a2, a3)
+                // ---------------- values: per k-step, rows 2t, 2t+1 (a0, a1) and 2t+8, 2t+9 (a2, a3)
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    const uint32_t ra = w == 0 ? vr[0].x : w == 1 ? vr[0].y : w == 2 ? vr[0].z : vr[0].w;
-                    const uint32_t rb = w == 0 ? vr[1].x : w == 1 ? vr[1].y : w == 2 ? vr[1].z : vr[1].w;
-                    const uint32_t rc = w == 0 ? vr[2].x : w == 1 ? vr[2].y : w == 2 ? vr[2].z : vr[2].w;
-                    const uint32_t rd = w == 0 ? vr[3].x : w == 1 ? vr[3].y : w == 2 ? vr[3].z : vr[3].w;
-                    uint32_t a0e, a1e, a0o, a1o, a2e, a3e, a2o, a3o;
-                    i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x5140), a0e, a1e);  // dims 4w, 4w+1
-                    i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x7362), a0o, a1o);  // dims 4w+2, 4w+3
-                    i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x5140), a2e, a3e);
-                    i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x7362), a2o, a3o);
-                    mma_16816<__half>(o[2 * w], a0e, a1e, a2e, a3e, pb0, pb1);
-                    mma_16816<__half>(o[2 * w + 1], a0o, a1o, a2o, a3o, pb0, pb1);
+                for (int vk = 0; vk < VK; ++vk) {
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        const uint4 *v4 = vr[vk];
+                        const uint32_t ra = w == 0 ? v4[0].x : w == 1 ? v4[0].y : w == 2 ? v4[0].z : v4[0].w;
+                        const uint32_t rb = w == 0 ? v4[1].x : w == 1 ? v4[1].y : w == 2 ? v4[1].z : v4[1].w;
+                        const uint32_t rc = w == 0 ? v4[2].x : w == 1 ? v4[2].y : w == 2 ? v4[2].z : v4[2].w;
+                        const uint32_t rd = w == 0 ? v4[3].x : w == 1 ? v4[3].y : w == 2 ? v4[3].z : v4[3].w;
+                        uint32_t a0e, a1e, a0o, a1o, a2e, a3e, a2o, a3o;
+                        i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x5140), a0e, a1e);  // dims 4w, 4w+1
+                        i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x7362), a0o, a1o);  // dims 4w+2, 4w+3
+                        i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x5140), a2e, a3e);
+                        i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x7362), a2o, a3o);
+                        mma_16816<__half>(o[2 * w], a0e, a1e, a2e, a3e, pb[2 * vk], pb[2 * vk + 1]);
+                        mma_16816<__half>(o[2 * w + 1], a0o, a1o, a2o, a3o, pb[2 * vk], pb[2 * vk + 1]);
+                    }
                 }
             }
             gidx += r.len;
@@ -1004,7 +1040,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             }
         } else {
             // ======== fp32 KV on the CUDA cores (packed FFMA).
-            static_assert(std::is_same<KV, float>::value, "the CUDA-core consumer serves fp32 KV");
+            static_assert(std::is_same<KV, float>::value && ROWS == 16,
+                          "the CUDA-core consumer serves fp32 KV in 16-token groups");
             // Stage q (G heads of this kv-head's group), scaled, as fp32.
             {
                 const long long qbase = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;

@@ -190,7 +190,6 @@ size_t prefill_lens_bytes(long long n) { return align_up(static_cast<uint32_t>(n
 // ------------------------------------------------------------------ fast path
 
 constexpr uint32_t kSmemBudget = 224 * 1024;
-constexpr int kMaxStagesPerWarp = 6;
 
 struct Launch {
     const void *fn;
@@ -204,18 +203,18 @@ struct Launch {
 // takes the one with more stages in flight: 7 when G = 8, whose per-warp merge buffers
 // crowd out stages), int8 and fp32 compile 11 and 8 (their consumers are latency-bound,
 // so 11 unless its stages do not fit).
-template <typename KV, int D, int G, int NC, bool SPLIT>
+template <typename KV, int D, int G, int NC, bool SPLIT, int ROWS>
 const void *fast_kernel() {
-    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, NC, SPLIT>);
+    return reinterpret_cast<const void *>(&decode_tma_kernel<KV, D, G, NC, SPLIT, ROWS>);
 }
 
-template <typename KV, int D, int NC, bool SPLIT>
+template <typename KV, int D, int NC, bool SPLIT, int ROWS = kRows>
 const void *pick_g(int G) {
     switch (G) {
-        case 1: return fast_kernel<KV, D, 1, NC, SPLIT>();
-        case 2: return fast_kernel<KV, D, 2, NC, SPLIT>();
-        case 4: return fast_kernel<KV, D, 4, NC, SPLIT>();
-        case 8: return fast_kernel<KV, D, 8, NC, SPLIT>();
+        case 1: return fast_kernel<KV, D, 1, NC, SPLIT, ROWS>();
+        case 2: return fast_kernel<KV, D, 2, NC, SPLIT, ROWS>();
+        case 4: return fast_kernel<KV, D, 4, NC, SPLIT, ROWS>();
+        case 8: return fast_kernel<KV, D, 8, NC, SPLIT, ROWS>();
         default: return nullptr;
     }
 }
@@ -238,7 +237,8 @@ NcList nc_candidates(int kv, int D) {
 // 16-bit KV computes on the tensor pipe; q wider than the MMA type (fp32 q, or any q
 // with f16 KV) is split into hi + lo halves (SPLIT).  int8 KV is turned into f16 on the
 // tensor pipe (fp32 q split); fp32 KV runs on packed FFMA.
-const void *pick_fast(int kv, int D, int G, bool q_f32, int nc) {
+const void *pick_fast(int kv, int D, int G, bool q_f32, int nc, int rows) {
+    if (rows != kRows && kv != GOLLEK_DTYPE_I8) return nullptr;
     switch (kv) {
         case GOLLEK_DTYPE_BF16:
             if (D == 128) {
@@ -258,6 +258,12 @@ const void *pick_fast(int kv, int D, int G, bool q_f32, int nc) {
             return nullptr;
         case GOLLEK_DTYPE_I8:
             if (D != 128) return nullptr;
+            if (rows == 32) {
+                if (q_f32) return nullptr;
+                if (nc == 11) return pick_g<int8_t, 128, 11, false, 32>(G);
+                if (nc == 8) return pick_g<int8_t, 128, 8, false, 32>(G);
+                return nullptr;
+            }
             if (nc == 11) return q_f32 ? pick_g<int8_t, 128, 11, true>(G) : pick_g<int8_t, 128, 11, false>(G);
             if (nc == 8) return q_f32 ? pick_g<int8_t, 128, 8, true>(G) : pick_g<int8_t, 128, 8, false>(G);
             return nullptr;
@@ -348,6 +354,16 @@ int encode_map3(CUtensorMap *m, const void *base, int kv, int D, long long rows)
     return GOLLEK_OK;
 }
 
+// Tokens per group and stage of the mma.sync kernel: int8 KV (head_dim 128) with bf16 q
+// and pages of at least 16 tokens moves 32-token groups, so that a stage holds as many
+// bytes as a 16-bit one and the per-group costs (block-table lookup, barriers, softmax
+// update) are paid half as often; everything else 16 (fp32 q's hi + lo fragments would
+// push 32-token groups past the register budget).
+int group_rows(const V2 &p) {
+    return (p.kv_dtype == GOLLEK_DTYPE_I8 && p.D == 128 && p.BS >= 16 &&
+            p.q_dtype == GOLLEK_DTYPE_BF16) ? 32 : kRows;
+}
+
 // Layout conditions shared by the TMA kernels (page tiles, alignment, sizes).
 bool tma_layout_ok(const V2 &p, long long page_stride) {
     const int eb = dtype_bytes(p.kv_dtype);
@@ -371,7 +387,7 @@ bool tma_layout_ok(const V2 &p, long long page_stride) {
 const void *fast_eligible(const V2 &p, int G, long long page_stride) {
     if (!tma_layout_ok(p, page_stride)) return nullptr;
     const NcList c = nc_candidates(p.kv_dtype, p.D);
-    return c.n ? pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c.v[0]) : nullptr;
+    return c.n ? pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c.v[0], group_rows(p)) : nullptr;
 }
 
 // Split-K scratch: the caller's workspace, or the library's per (device, stream) one;
@@ -389,18 +405,19 @@ int v2_workspace(const V2 &p, int dev, void **ws, size_t *cap) {
 }
 
 // 2-D tensor maps over the K and V pools: rows of head_dim elements, boxes of 128 bytes
-// x min(block_size, 16) rows.
-int v2_maps(const V2 &p, long long page_stride, CUtensorMap *tmk, CUtensorMap *tmv) {
+// x min(block_size, group rows) rows.
+int v2_maps(const V2 &p, long long page_stride, int group, CUtensorMap *tmk, CUtensorMap *tmv) {
     const long long rows_per_page = page_stride / p.D;
     const long long rows =
         p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page : (1LL << 31) - 1;
-    const int box_rows = p.BS < kRows ? p.BS : kRows;
+    const int box_rows = p.BS < group ? p.BS : group;
     int rc = encode_map(tmk, p.k, p.kv_dtype, p.D, rows, box_rows);
     if (!rc) rc = encode_map(tmv, p.v, p.kv_dtype, p.D, rows, box_rows);
     return rc;
 }
 
-DecodeArgs v2_args(const V2 &p, void *ws, size_t ws_cap, long long page_stride, int stages) {
+DecodeArgs v2_args(const V2 &p, void *ws, size_t ws_cap, long long page_stride, int stages,
+                   int group = kRows) {
     const bool cap = p.soft_cap > 0.f;
     DecodeArgs a;
     a.out = p.out;
@@ -426,9 +443,10 @@ DecodeArgs v2_args(const V2 &p, void *ws, size_t ws_cap, long long page_stride, 
     a.num_vstages = 0;
     a.box3d = 0;
     a.seq_div = p.seq_div > 1 ? p.seq_div : 1;
+    a.group_rows = group;
     a.scale_mode = 2;
     if (p.kv_dtype == GOLLEK_DTYPE_I8) {
-        const int R = p.BS < kRows ? p.BS : kRows;
+        const int R = p.BS < group ? p.BS : group;
         if (p.sts == 1 && (p.sps * 4) % 16 == 0 && (p.shs * 4) % 16 == 0 && aligned16(p.ks) &&
             aligned16(p.vs) && (R * 4) % 16 == 0)
             a.scale_mode = 0;
@@ -539,7 +557,8 @@ int run_v2(const V2 &p) {
     if (fn) {
         const int eb = dtype_bytes(p.kv_dtype);
         const bool quant = p.kv_dtype == GOLLEK_DTYPE_I8;
-        const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * kSlabBytes;
+        const int rows = group_rows(p);
+        const uint32_t tile = static_cast<uint32_t>(p.D * eb / 128) * rows * 128;
         const int max_ctas = sm_count(dev) * 2;
         // warp count: 16-bit KV takes the candidate with the most stages in flight, int8
         // and fp32 the first that fits
@@ -550,12 +569,12 @@ int run_v2(const V2 &p) {
         fn = nullptr;
         for (int ci = 0; ci < cand.n; ++ci) {
             const int c = cand.v[ci];
-            const void *f = pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c);
+            const void *f = pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c, rows);
             if (!f) continue;
-            DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, c, 0, p.S, max_ctas);
+            DecodeSmem L0 = decode_smem_layout(eb, quant, p.D, G, c, 0, p.S, max_ctas, rows);
             int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / (2 * tile * c));
             spw = std::min(std::max(spw, 1), kMaxStagesPerWarp);
-            DecodeSmem Lc = decode_smem_layout(eb, quant, p.D, G, c, spw * c, p.S, max_ctas);
+            DecodeSmem Lc = decode_smem_layout(eb, quant, p.D, G, c, spw * c, p.S, max_ctas, rows);
             if (Lc.total > 227 * 1024) continue;
             // TMA and bulk-copy destinations and vector accesses need these alignments
             if (Lc.q % 16 || Lc.p % 16 || Lc.scales % 16 || Lc.rstart % 8 || Lc.bars % 8) continue;
@@ -573,17 +592,17 @@ int run_v2(const V2 &p) {
             int rc = v2_workspace(p, dev, &ws, &ws_cap);
             if (rc) return rc;
             CUtensorMap tmk, tmv;
-            const bool box3d = p.BS >= kRows && p.D * eb >= 256;
+            const bool box3d = rows == kRows && p.BS >= kRows && p.D * eb >= 256;
             if (box3d) {
                 const long long rows = p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * (page_stride / p.D)
                                                         : (1LL << 31) - 1;
                 rc = encode_map3(&tmk, p.k, p.kv_dtype, p.D, rows);
                 if (!rc) rc = encode_map3(&tmv, p.v, p.kv_dtype, p.D, rows);
             } else {
-                rc = v2_maps(p, page_stride, &tmk, &tmv);
+                rc = v2_maps(p, page_stride, rows, &tmk, &tmv);
             }
             if (rc) return rc;
-            DecodeArgs a = v2_args(p, ws, ws_cap, page_stride, stages);
+            DecodeArgs a = v2_args(p, ws, ws_cap, page_stride, stages, rows);
             a.box3d = box3d ? 1 : 0;
 
             GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),

@@ -405,7 +405,7 @@ def test_int8_scales_spanning_decades(cuda_device):
         assert (err <= bound).all(), (per_token, float((err / bound).max()))
 
 
-@pytest.mark.parametrize("bs", [8, 32])
+@pytest.mark.parametrize("bs", [8, 16, 32, 64])
 def test_int8_block_sizes(cuda_device, bs):
     ctx = [3, 77, 640]
     q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=bs, seed=27, kv_std=0.5)
