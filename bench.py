@@ -412,47 +412,62 @@ def bench_decode(args, world, rank, local):
 
     for name, t in parts:
         view(h_stage, name, t).copy_(t)
-    d = {name: view(d_stage, name, t) for name, t in parts}
     hout_pin = torch.empty(batch.out.shape, dtype=batch.out.dtype).pin_memory()
     ws_e2e = torch.zeros(_lib.load().gollek_paged_attention_workspace_size(B, Hq, batch.hkv, D),
                          dtype=torch.uint8, device=dev)
 
-    def e2e_step():
-        d_stage.copy_(h_stage, non_blocking=True)
+    # The steps run as a double-buffered pipeline, the way a serving loop overlaps its
+    # transfers with compute: step k's inputs go up on a copy stream (into staging buffer
+    # k % 2) while step k-1 decodes, and step k's output comes down on a second copy
+    # stream while step k+1 decodes.  Every step still copies its own inputs in and its
+    # own result out; the append and the decode of consecutive steps stay in order on the
+    # compute stream.
+    s_comp = stream
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    d_stages = [d_stage, torch.empty_like(d_stage)]
+    dv = [{name: view(buf, name, t) for name, t in parts} for buf in d_stages]
+    outs = [batch.out, torch.empty_like(batch.out)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def pipe_step(k, after=None):
+        b = k % 2
+        dd = dv[b]
+        with torch.cuda.stream(s_in):
+            if after is not None:
+                s_in.wait_event(after)
+            if k >= 2:
+                s_in.wait_event(ev_used[b])  # step k-2's decode has read this staging buffer
+            d_stages[b].copy_(h_stage, non_blocking=True)
+            ev_in[b].record(s_in)
+        s_comp.wait_event(ev_in[b])
+        if k >= 2:
+            s_comp.wait_event(ev_out[b])  # step k-2's output has been copied out
         if append:
-            ops.kv_append(d["k_new"], d["v_new"], d["pos"], d["bt"], batch.k, batch.v,
-                          block_size=batch.sh["bs"], num_blocks=batch.nb)
-        batch.run(q=d["q"], bt=d["bt"], ctx=d["ctx"], workspace=ws_e2e)
-        hout_pin.copy_(batch.out, non_blocking=True)
+            ops.kv_append(dd["k_new"], dd["v_new"], dd["pos"], dd["bt"], batch.k, batch.v,
+                          block_size=batch.sh["bs"], num_blocks=batch.nb, stream=s_comp)
+        batch.run(out=outs[b], q=dd["q"], bt=dd["bt"], ctx=dd["ctx"], workspace=ws_e2e, stream=s_comp)
+        ev_used[b].record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_used[b])
+            hout_pin.copy_(outs[b], non_blocking=True)
+            ev_out[b].record(s_out)
 
-    # The step (copy in, append, decode, copy out) replays as one CUDA graph when it
-    # captures; otherwise it runs eagerly.
-    e2e_graph, graph_note = None, "eager"
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    try:
-        cg = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(cg):
-            e2e_step()
-        torch.cuda.synchronize()
-        e2e_graph, graph_note = cg, "CUDA graph of the step"
-    except Exception as exc:  # capture refused: run the same calls eagerly
-        torch.cuda.synchronize()
-        graph_note = f"eager (graph capture failed: {str(exc)[:80]})"
-    step_fn = e2e_graph.replay if e2e_graph is not None else e2e_step
-
+    graph_note = ("double-buffered pipeline on 3 streams: H2D of step k+1 and D2H of step k-1 "
+                  "overlap the decode of step k")
     e2e_steps = max(1, min(args.steps, 100))
-    for _ in range(args.warmup):
-        step_fn()
+    for k in range(max(2, args.warmup)):
+        pipe_step(k)
     torch.cuda.synchronize()
     barrier(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     w0 = time.perf_counter()
-    f0.record(stream)
-    for _ in range(e2e_steps):
-        step_fn()
-    f1.record(stream)
+    f0.record(s_comp)
+    for k in range(e2e_steps):
+        pipe_step(k, after=f0 if k == 0 else None)
+    s_comp.wait_event(ev_out[(e2e_steps - 1) % 2])
+    f1.record(s_comp)
     torch.cuda.synchronize()
     wall = time.perf_counter() - w0
     barrier(world)
