@@ -1,7 +1,8 @@
 """Benchmark of the paged-KV hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode_bf16|decode_int8|decode_fp32|longctx|migrate]
+                    [--workload decode_bf16|decode_int8|decode_fp32|longctx|migrate|config1|
+                                prefill|cow] [--tq T]
 
 Default workload: Llama-3-8B-shaped bf16 decode attention, 32 query
 heads over 8 KV heads, head_dim 128, block 16, 64 sequences with context lengths
@@ -11,7 +12,10 @@ batch (sequences are independent units; no collective on the data path): weak sc
 
 Other workloads (run by hand, one JSON line each): decode_int8 (config 3), decode_fp32,
 longctx (config 5, KV heads sharded over the ranks, strong scaling), migrate (config 4,
-prefill ranks push KV blocks to decode ranks over NVLink).
+prefill ranks push KV blocks to decode ranks over NVLink), config1 (the legacy fp32
+symbol on config 1), prefill (multi-query causal attention, T query tokens per sequence
+over config 2's pool), cow (prompt-cache copy-on-write block copy inside one GPU's pool,
+config 4's block layout).
 
 --impl reference times the reference's own CPU algorithm for the same workload: the
 C restatement in oracle/ (the reference is Java; no JDK exists here), all host threads.
@@ -42,7 +46,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode_bf16",
-                    choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate", "config1"])
+                    choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate", "config1",
+                             "prefill", "cow"])
+    ap.add_argument("--tq", type=int, default=4, help="prefill: query tokens per sequence")
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--gather", action="store_true", help="longctx: all-gather head-sharded outputs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -287,13 +293,16 @@ def sum_over_ranks(x, world):
 
 # ------------------------------------------------------------------ CPU baseline
 
-def cpu_decode_baseline(batch, seconds, threads=None):
+def cpu_decode_baseline(batch, seconds, threads=None, q=None, tq=1):
     """The reference's CPU algorithm (oracle restatement of PagedAttentionVectorAPI) on
-    fp32 copies of the same values, all host threads, whole batch per step."""
+    fp32 copies of the same values, all host threads, whole batch per step.  q/tq: a
+    multi-query step ([S, tq, Hq, D] queries at each sequence's last tq positions)."""
     import numpy as np
     from oracle import oracle as O
     threads = threads or O.num_threads()
-    q = batch.q.float().cpu().numpy()
+    q = (batch.q if q is None else q).float().cpu().numpy()
+    if q.ndim == 3:
+        q = q[:, None]
     bt, ctx = batch.bt_np, batch.ctx_np
     # int8 pages: the oracle's INT8 storage with per-token scales (the page scale repeated)
     if batch.k_scales is not None:
@@ -314,7 +323,7 @@ def cpu_decode_baseline(batch, seconds, threads=None):
     n = 1
     while True:
         t0 = time.perf_counter()
-        O.a2_compute(q[:n, None], k, v, bt[:n], ctx[:n], scale, storage=storage,
+        O.a2_compute(q[:n], k, v, bt[:n], ctx[:n], scale, storage=storage,
                      num_kv_heads=batch.hkv, block_size=batch.sh["bs"], k_scale=ks, v_scale=vs,
                      threads=threads)
         dt = time.perf_counter() - t0
@@ -324,7 +333,7 @@ def cpu_decode_baseline(batch, seconds, threads=None):
     reps, total, t_start = 0, 0.0, time.perf_counter()
     while time.perf_counter() - t_start < seconds and reps < 1000:
         t0 = time.perf_counter()
-        O.a2_compute(q[:n, None], k, v, bt[:n], ctx[:n], scale, storage=storage,
+        O.a2_compute(q[:n], k, v, bt[:n], ctx[:n], scale, storage=storage,
                      num_kv_heads=batch.hkv, block_size=batch.sh["bs"], k_scale=ks, v_scale=vs,
                      threads=threads)
         total += time.perf_counter() - t0
@@ -333,7 +342,8 @@ def cpu_decode_baseline(batch, seconds, threads=None):
     # tokens/s over the whole batch: the sample's time per sequence, weighted by context
     frac = float(ctx[:n].sum()) / float(ctx.sum())
     t_step = (total / reps) / frac
-    return {"value": B / t_step, "unit": "tokens/s", "cores": int(threads), "kind": "port",
+    return {"value": B * tq / t_step, "unit": "tokens/s" if tq == 1 else "query tokens/s",
+            "cores": int(threads), "kind": "port",
             "sample": f"{n} of {B} sequences ({frac:.1%} of the batch's context tokens), "
                       f"{reps} repetitions, {total:.1f} s; scaled to the full batch by context "
                       f"tokens; oracle/oracle.c a2 (PagedAttentionVectorAPI restatement), "
@@ -820,6 +830,187 @@ def cpu_migrate_baseline(seed, seconds=3.0, sample_blocks=128):
                       "oracle/oracle.c oracle_migrate, the reference's sequential copy loop"}
 
 
+# ------------------------------------------------------------------ multi-query and CoW benches
+
+def timed_steps(step, args, world, local, stream):
+    """Warm-up, then args.steps steps between CUDA events on `stream` (barrier and
+    synchronize on both sides); returns (this rank's ms, max over ranks, clock summary)."""
+    import torch
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_ms = e0.elapsed_time(e1)
+    return t_ms, max_over_ranks(t_ms, world), clk.summary()
+
+
+def bench_prefill(args, world, rank, local):
+    """Multi-query paged attention (gollek_paged_attention_prefill; the reference's
+    PagedAttentionVectorAPI.compute with seqLenQ > 1): config 2's batch and pool with
+    --tq query tokens per sequence at its last positions, causal -- speculative
+    verification or a short prefill chunk.  value = query tokens/s.  The roofline
+    numerator counts each context token's K/V once per step (what a kernel reading every
+    page once must move); the kernel reads a sequence's pages once per query, the repeats
+    of adjacent queries largely served from L2, so traffic shows how much reaches HBM."""
+    import torch
+    from gollek_b200 import _lib, ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    batch = DecodeBatch("decode_bf16", args.seed + rank, dev)
+    B, Hq, D = batch.q.shape
+    Tq = args.tq
+    g = torch.Generator(device=dev).manual_seed(args.seed + 11 + rank)
+    q = torch.randn((B, Tq, Hq, D), generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    lib = _lib.load()
+    ws = torch.zeros(lib.gollek_paged_attention_prefill_workspace_size(B, Tq, Hq, batch.hkv, D),
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def run(qd, od, bt, ctx):
+        ops.paged_attention_prefill(qd, batch.k, batch.v, bt, ctx, num_kv_heads=batch.hkv,
+                                    block_size=batch.sh["bs"], num_blocks=batch.nb, causal=True,
+                                    out=od, workspace=ws, stream=stream)
+
+    t_ms, t_max, clocks = timed_steps(lambda: run(q, out, batch.bt, batch.ctx), args, world, local,
+                                      stream)
+    # e2e: q, tables and lengths from pinned host memory, output back to pinned host memory
+    hq_ = q.cpu().pin_memory()
+    hbt, hctx = batch.bt.cpu().pin_memory(), batch.ctx.cpu().pin_memory()
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dq, dbt, dctx = torch.empty_like(q), torch.empty_like(batch.bt), torch.empty_like(batch.ctx)
+
+    def e2e_step():
+        dq.copy_(hq_, non_blocking=True)
+        dbt.copy_(hbt, non_blocking=True)
+        dctx.copy_(hctx, non_blocking=True)
+        run(dq, out, dbt, dctx)
+        hout.copy_(out, non_blocking=True)
+
+    class _E2E:
+        steps, warmup = max(1, min(args.steps, 100)), args.warmup
+    e_ms, e_max, _ = timed_steps(e2e_step, _E2E, world, local, stream)
+    h2d = sum(t.numel() * t.element_size() for t in (hq_, hbt, hctx))
+    d2h = hout.numel() * hout.element_size()
+
+    kv_once = batch.algorithmic_bytes() - 2 * batch.q.numel() * batch.q_elem
+    alg = kv_once + 2 * q.numel() * q.element_size()
+    achieved = alg / ((t_ms / 1e3) / args.steps) / 1e9
+    achieved_min = -max_over_ranks(-achieved, world)
+    peak, peak_kind = peaks()
+    value = B * Tq * world * args.steps / (t_max / 1e3)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_decode_baseline(batch, args.cpu_seconds, q=q, tq=Tq)
+        cpu.pop("per_seq_s", None)
+        cpu.pop("seconds_per_step", None)
+    if rank == 0:
+        sh = batch.sh
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": "query tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 KV/q/out, f32 accumulate", "data": "synthetic (seeded; config 2 shapes)",
+            "config": {"workload": f"multi_query_causal_tq{Tq}_config2_pool", "batch_per_gpu": B,
+                       "queries_per_seq": Tq, "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"],
+                       "head_dim": sh["d"], "block_size": sh["bs"],
+                       "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
+                       "parallelism": f"independent batches x{world}",
+                       "l2": f"no flush: {kv_once / 1e9:.2f} GB of KV per step per GPU > 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
+                         "frac": achieved_min / peak, "traffic": None,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                         "algorithmic_bytes_per_launch": alg,
+                         "note": "numerator counts each page once per step (page-once ideal)",
+                         "kernel": "decode_tma_kernel (per-query decode sequences)"},
+            "e2e": {"value": B * Tq * world * _E2E.steps / (e_max / 1e3), "unit": "query tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": _E2E.steps,
+                    "path": "pinned q, tables, lengths -> H2D -> gollek_paged_attention_prefill "
+                            "-> D2H of out, serialised on one stream"},
+            "gpu_launches": 2 * args.steps, "clocks": clocks, "cpu_baseline": cpu,
+        }), flush=True)
+
+
+def bench_cow(args, world, rank, local):
+    """Prompt-cache copy-on-write block copy (the per-(block, layer) copy of
+    optimization/gollek-plugin-prompt-cache PagedKVCacheManagerExtension.java:170-180):
+    gollek_kv_migrate with source and destination in one GPU's pool.  Config 4's block
+    layout (32 layers x 32 KiB per block, 1 MiB per block for each of K and V); each step
+    copies the blocks of a quarter of config 4's requests to a permuted set of free
+    blocks of the same pool.  value = GB/s copied; the HBM roofline counts the bytes read
+    plus the bytes written, like the measured copy peak."""
+    import numpy as np
+    import torch
+    from gollek_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    L, H, BS, D = 32, 8, 16, 128
+    blk = L * BS * H * D * 2
+    lens, src_rank, blocks, _ = migrate_plan(args.seed, 8)
+    nblk = int(blocks[src_rank == 0].sum())
+    rng = np.random.default_rng(args.seed + 300 + rank)
+    pool_blocks = 2 * nblk + 64
+    perm = rng.permutation(pool_blocks).astype(np.int32)
+    src_ids, dst_ids = perm[:nblk], perm[nblk:2 * nblk]
+    k = torch.empty(pool_blocks * blk, dtype=torch.uint8, device=dev)
+    v = torch.empty_like(k)
+    gen = torch.Generator(device=dev).manual_seed(args.seed + rank)
+    for t in (k, v):
+        fl = t.view(torch.bfloat16)
+        step_n = 1 << 28
+        for i in range(0, fl.numel(), step_n):
+            n = min(step_n, fl.numel() - i)
+            fl[i:i + n] = torch.randn(n, generator=gen, device=dev).to(torch.bfloat16)
+    s_ids, d_ids = torch.from_numpy(src_ids).to(dev), torch.from_numpy(dst_ids).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ops.kv_migrate(k, v, k, v, s_ids, d_ids, src_block_stride=blk, dst_block_stride=blk,
+                       bytes_per_block=blk, device=local)
+
+    t_ms, t_max, clocks = timed_steps(step, args, world, local, stream)
+    same = all(torch.equal(ops.block_checksums(p, s_ids, block_stride=blk, bytes_per_block=blk),
+                           ops.block_checksums(p, d_ids, block_stride=blk, bytes_per_block=blk))
+               for p in (k, v))
+    ok = -max_over_ranks(-float(same), world) > 0.5
+    copied = nblk * blk * 2
+    gbs = copied / ((t_ms / 1e3) / args.steps) / 1e9
+    gbs_min = -max_over_ranks(-gbs, world)
+    peak, peak_kind = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_migrate_baseline(args.seed)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": copied * world * args.steps / (t_max / 1e3) / 1e9,
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8 (bf16 KV bytes)",
+            "data": "synthetic (seeded; config 4 block layout)",
+            "config": {"workload": "prompt_cache_cow_block_copy_config4_layout", "layers": L,
+                       "kv_heads": H, "head_dim": D, "block_size": BS, "blocks_per_step": nblk,
+                       "bytes_copied_per_step": copied,
+                       "parallelism": f"independent pools x{world}",
+                       "l2": f"no flush: {copied / 1e9:.1f} GB copied per step > 126 MB L2"},
+            "bit_exact": bool(ok),
+            "roofline": {"bound": "hbm", "achieved": 2 * gbs_min, "peak": peak, "unit": "GB/s",
+                         "frac": 2 * gbs_min / peak, "traffic": None,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind}); achieved "
+                                        "counts read + write bytes",
+                         "kernel": "kv_migrate_kernel_v16"},
+            "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": cpu,
+        }), flush=True)
+
+
 # ------------------------------------------------------------------ reference arm
 
 def bench_reference(args):
@@ -933,6 +1124,10 @@ def main():
             bench_migrate(args, world, rank, local)
         elif args.workload == "config1":
             bench_config1(args, world, rank, local)
+        elif args.workload == "prefill":
+            bench_prefill(args, world, rank, local)
+        elif args.workload == "cow":
+            bench_cow(args, world, rank, local)
         else:
             bench_decode(args, world, rank, local)
     finally:

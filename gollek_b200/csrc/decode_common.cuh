@@ -47,6 +47,9 @@ struct DecodeArgs {
     int num_vstages;      // tensor-memory kernel: V tiles
     int box3d;            // 1: one 3-D TMA box (all 128-byte slabs of 16 rows) per page
     int seq_div;          // block-table row of sequence s is s / seq_div (queries of one sequence)
+    int qfold;            // > 1: the G rows of (s, h) are qfold queries x G/qfold heads of one
+                          // chunk of seq_div chunks (qo_row); the chunk's query i < qfold sees
+                          // the positions before len - (qfold - 1 - i)
     int group_rows;       // tokens per group: 16, or 32 (int8 kernel with 32-token stages)
     int scale_mode;       // int8: 0 per-token scales by bulk copy, 1 one scale per page, 2 general
     float q_scale;        // applied to q when staged: scale*log2(e), or scale with soft-cap
@@ -56,6 +59,19 @@ struct DecodeArgs {
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
+
+// Row of q/out (in units of head_dim elements) holding row g of the G rows of (decode
+// sequence v, kv-head h).  Decode: q/out [S, Hkv*G, D], row (v*Hkv + h)*G + g.  Folded
+// multi-query (F = qfold > 1): sequence s has C = seq_div chunks v = s*C + c of F queries,
+// the G rows of a chunk are its F queries x G/F heads, and q/out are [S, C*F, Hkv*G/F, D].
+__device__ __forceinline__ long long qo_row(int v, int h, int g, int Hkv, int G, int F, int C) {
+    if (F <= 1) return (static_cast<long long>(v) * Hkv + h) * G + g;
+    const int gm = G / F;
+    const int s = v / C;
+    const int qi = g / gm;
+    const int i = (v - s * C) * F + qi;
+    return ((static_cast<long long>(s) * C * F + i) * Hkv + h) * gm + (g - qi * gm);
+}
 
 __device__ __forceinline__ void store_out(void *out, long long idx, float v, int bf16) {
     if (bf16)

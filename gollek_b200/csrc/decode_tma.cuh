@@ -519,7 +519,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     qa[kk][1] = qnext[kk][1];
                 }
             } else {
-                const long long qrow = ((static_cast<long long>(r.s) * Hkv + r.h) * G + g) * D;
+                const long long qrow = qo_row(r.s, r.h, g < G ? g : 0, Hkv, G, a.qfold, a.seq_div) * D;
                 float qx[KS][2][2];
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
@@ -578,6 +578,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float o[KS][4];           // O^T fragments: d = 16*mt + g (+8), heads 2t, 2t+1
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+            // Folded multi-query rows: row g is query g / (G / qfold), which sees the
+            // positions before len - qshift.
+            const int qshift = (a.qfold > 1 && g < G) ? a.qfold - 1 - g / (G / a.qfold) : 0;
             // ldmatrix row address of lane: token r + 8*(i>>1), 8 columns at 8*(i&1)
             const int lm_tok = (lane & 7) + 8 * (lane >> 4);
             const int lm_col = 8 * ((lane >> 3) & 1);
@@ -643,6 +646,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
+                // (folded queries: row g's query sees qshift fewer positions than the last)
+                const int row_hi = min(v_hi, sw.len - qshift - t0);
                 float p[2][2];
                 float mloc = -INFINITY;
 #pragma unroll
@@ -657,7 +662,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         } else {
                             x2 *= qmul;
                         }
-                        x2 = (tk >= v_lo && tk < v_hi) ? x2 : -INFINITY;
+                        x2 = (tk >= v_lo && tk < row_hi) ? x2 : -INFINITY;
                         p[nt][e] = x2;
                         mloc = fmaxf(mloc, x2);
                     }
@@ -702,7 +707,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (have_qnext) {
                     const Run rn = run_at(x);
                     const uint32_t *qw = reinterpret_cast<const uint32_t *>(a.q) +
-                                         ((static_cast<long long>(rn.s) * Hkv + rn.h) * G + g) * (D / 2);
+                                         qo_row(rn.s, rn.h, g < G ? g : 0, Hkv, G, a.qfold, a.seq_div) * (D / 2);
 #pragma unroll
                     for (int kk = 0; kk < KS; ++kk) {
                         qnext[kk][0] = g < G ? __ldg(qw + 8 * kk + t) : 0u;
@@ -1233,6 +1238,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         if (*cons_abort) break;  // a wait gave up in this CTA: stop cleanly
 
         const long long out_row = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
+        // element o of the (s, h) state [G][D] in out (folded queries: [S, qfold, Hq, D])
+        auto out_at = [&](int o) -> long long {
+            return a.qfold > 1 ? qo_row(r.s, r.h, o / D, Hkv, G, a.qfold, a.seq_div) * D + (o % D) : out_row + o;
+        };
         const int slot_floats = 2 * G + G * D;
         float *part = nullptr;
         if (r.pieces > 1)
@@ -1256,7 +1265,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             }
             if (r.pieces == 1) {
                 const float v = Ls > 0.f ? As * (1.0f / (Ls + a.norm_eps)) : 0.f;
-                store_out(a.out, out_row + o, v, a.q_bf16);
+                store_out(a.out, out_at(o), v, a.q_bf16);
             } else {
                 part[2 * G + o] = As;
                 if ((o % D) == 0) {
@@ -1292,7 +1301,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         }
                     }
                     const float v = Ls > 0.f ? As * (1.0f / (Ls + a.norm_eps)) : 0.f;
-                    store_out(a.out, out_row + o, v, a.q_bf16);
+                    store_out(a.out, out_at(o), v, a.q_bf16);
                 }
                 if (tid == 0) atomicExch(&a.counters[r.s * Hkv + r.h], 0);
             }

@@ -172,16 +172,19 @@ size_t ws_bytes(int S, int Hq, int Hkv, int D) {
     return P + P / 64 + 1024;
 }
 
-// Multi-query attention as decode: query i of sequence s (absolute position
-// ctx[s] - Tq + i, PagedAttentionVectorAPI.compute) becomes sequence s*Tq + i with
-// context length ctx[s] - Tq + i + 1 when causal, ctx[s] otherwise.
-__global__ void prefill_lengths_kernel(const int *ctx, int *lens, int S, int Tq, int causal) {
-    const long long n = static_cast<long long>(S) * Tq;
+// Multi-query attention as decode: the Tq = C*F queries of sequence s (query i at
+// absolute position ctx[s] - Tq + i, PagedAttentionVectorAPI.compute) become C decode
+// sequences s*C + c of F queries each (F > 1: folded into the kernel's rows next to the
+// GQA heads).  Chunk c's length is that of its last query, ctx[s] - Tq + (c+1)*F, when
+// causal, ctx[s] otherwise.
+__global__ void prefill_lengths_kernel(const int *ctx, int *lens, int S, int C, int F, int causal) {
+    const long long n = static_cast<long long>(S) * C;
+    const int Tq = C * F;
     for (long long v = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; v < n;
          v += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int s = static_cast<int>(v / Tq), i = static_cast<int>(v % Tq);
-        const int c = ctx[s];
-        lens[v] = (causal && c >= 0) ? max(0, c - Tq + i + 1) : c;  // negative stays: BAD_POSITION
+        const int s = static_cast<int>(v / C), c = static_cast<int>(v % C);
+        const int x = ctx[s];
+        lens[v] = (causal && x >= 0) ? max(0, x - Tq + (c + 1) * F) : x;  // negative stays: BAD_POSITION
     }
 }
 
@@ -299,6 +302,7 @@ struct V2 {
     size_t workspace_bytes;
     void *stream;
     int seq_div;  // > 1: S counts (sequence, query) pairs, block-table row = s / seq_div
+    int qfold;    // > 1: folded multi-query call, Hq counts qfold queries x the model's q heads
 };
 
 int encode_map(CUtensorMap *m, const void *base, int kv, int D, long long rows, int box_rows) {
@@ -443,6 +447,7 @@ DecodeArgs v2_args(const V2 &p, void *ws, size_t ws_cap, long long page_stride, 
     a.num_vstages = 0;
     a.box3d = 0;
     a.seq_div = p.seq_div > 1 ? p.seq_div : 1;
+    a.qfold = p.qfold > 1 ? p.qfold : 1;
     a.group_rows = group;
     a.scale_mode = 2;
     if (p.kv_dtype == GOLLEK_DTYPE_I8) {
@@ -493,6 +498,7 @@ constexpr int kNotTaken = 1 << 30;
 // kNotTaken when the case is outside its range.
 int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     const DecodePath mode = decode_path();
+    if (p.qfold > 1) return kNotTaken;  // folded queries: the mma.sync kernel only
     if (mode == DecodePath::kMma || p.kv_dtype != GOLLEK_DTYPE_BF16 || p.D != 128) return kNotTaken;
     if (mode == DecodePath::kAuto && fast_eligible(p, G, page_stride)) return kNotTaken;
     if (!tma_layout_ok(p, page_stride) || !aligned16(p.q)) return kNotTaken;
@@ -619,6 +625,9 @@ int run_v2(const V2 &p) {
         }
     }
 
+    // Folded multi-query calls run on the mma.sync kernel or not at all (the caller then
+    // runs the queries as separate decode sequences).
+    if (p.qfold > 1) return kNotTaken;
     // Generic kernel.
     if (G > kGenMaxG || p.D > kGenMaxJ * 32)
         return fail(GOLLEK_ERR_UNSUPPORTED, "head_dim %d / GQA group %d outside the supported range",
@@ -844,6 +853,11 @@ size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_heads, int 
     return ws_bytes(num_seqs, num_q_heads, num_kv_heads, head_dim);
 }
 
+static bool prefill_fold_enabled() {
+    const char *e = std::getenv("GOLLEK_PREFILL_FOLD");
+    return !(e && e[0] == '0');
+}
+
 size_t gollek_paged_attention_prefill_workspace_size(int num_seqs, int num_queries, int num_q_heads,
                                                      int num_kv_heads, int head_dim) {
     if (num_seqs <= 0 || num_queries <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 ||
@@ -920,14 +934,40 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
         return fail(GOLLEK_ERR_WORKSPACE, "workspace of %zu bytes too small", cap);
     int *lens = reinterpret_cast<int *>(static_cast<uint8_t *>(ws) + (cap - lens_bytes) / 256 * 256);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int threads = 256;
-    const int blocks = static_cast<int>(std::min<long long>((n + threads - 1) / threads, 4096));
-    prefill_lengths_kernel<<<blocks, threads, 0, st>>>(context_lens, lens, num_seqs, num_queries, causal);
-    GK_CUDA(cudaGetLastError(), "prefill_lengths_kernel launch");
     p.ctx = lens;
     p.workspace = ws;
     p.workspace_bytes = cap;
-    return run_v2(p);
+    // Page-once chunks: F queries of a sequence times its GQA group G as the rows of one
+    // (sequence, kv-head) unit of the 16-bit mma.sync kernel (G*F one of its row counts
+    // 2, 4, 8), each row with its own causal limit, so a page is read once per F queries
+    // instead of once per query.  Causal, no sliding window (its start would differ per
+    // row), bf16/f16 KV.  F is the largest such divisor of Tq; GOLLEK_PREFILL_FOLD=0 keeps
+    // one query per decode sequence.  The partial slots need the same bytes either way.
+    const int G = num_q_heads / num_kv_heads;
+    int F = 1;
+    if (causal && sliding_window <= 0 && prefill_fold_enabled() &&
+        (kv_dtype == GOLLEK_DTYPE_BF16 || kv_dtype == GOLLEK_DTYPE_F16))
+        for (int f = 8 / std::max(G, 1); f > 1; f >>= 1)
+            if (num_queries % f == 0 && G * f <= 8) {
+                F = f;
+                break;
+            }
+    for (;;) {
+        const int C = num_queries / F;
+        const long long nv = static_cast<long long>(num_seqs) * C;
+        const int threads = 256;
+        const int blocks = static_cast<int>(std::min<long long>((nv + threads - 1) / threads, 4096));
+        prefill_lengths_kernel<<<blocks, threads, 0, st>>>(context_lens, lens, num_seqs, C, F, causal);
+        GK_CUDA(cudaGetLastError(), "prefill_lengths_kernel launch");
+        p.S = static_cast<int>(nv);
+        p.Hq = num_q_heads * F;
+        p.seq_div = C;
+        p.qfold = F;
+        rc = run_v2(p);
+        if (rc != kNotTaken || F == 1) return rc;
+        t_last_error.clear();
+        F = 1;  // the folded kernel was not available for this case: one query per sequence
+    }
 }
 
 int gollek_paged_attention_v2_noalloc(void *out, const void *q, const void *k_cache,

@@ -109,3 +109,55 @@ def test_prefill_refuses_window_without_causal(cuda_device):
                                     block_size=16, causal=False, sliding_window=16,
                                     num_blocks=k.shape[0])
     assert e.value.code == _lib.ERR_UNSUPPORTED
+
+
+def _prefill(q, k, v, bt, ctx, dev, *, hkv, q_dtype, kv_dtype, scale):
+    from gollek_b200 import ops
+    return ops.paged_attention_prefill(_t(q, dev, q_dtype), _t(k, dev, kv_dtype), _t(v, dev, kv_dtype),
+                                       _t(bt, dev), _t(ctx, dev), num_kv_heads=hkv, block_size=16,
+                                       scale=scale, causal=True, num_blocks=k.shape[0])
+
+
+@pytest.mark.parametrize("hq,hkv,tq", [(32, 8, 2), (32, 8, 4), (32, 8, 8), (8, 8, 8), (16, 8, 4),
+                                       (16, 8, 6), (64, 8, 2)])
+def test_prefill_page_once_chunks(cuda_device, monkeypatch, hq, hkv, tq):
+    """Causal bf16 multi-query calls whose queries fold into the decode kernel's rows
+    (F queries x G heads <= 8 per page read, F the largest power of two dividing Tq):
+    against the oracle, and against the same call with folding turned off
+    (GOLLEK_PREFILL_FOLD=0: one decode sequence per query).  Lengths below Tq give queries
+    that see nothing (zeros); 6000 tokens split across CTAs (split-K merge per row)."""
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([2, 5, 17, 300, 2100, 6000], tq, hq, hkv, seed=70 + tq + hq)
+    qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=16, causal=1)
+    folded = [_prefill(qb, kb, vb, bt, ctx, cuda_device, hkv=hkv, q_dtype=torch.bfloat16,
+                       kv_dtype=torch.bfloat16, scale=scale).float().cpu().numpy() for _ in range(2)]
+    monkeypatch.setenv("GOLLEK_PREFILL_FOLD", "0")
+    per_query = _prefill(qb, kb, vb, bt, ctx, cuda_device, hkv=hkv, q_dtype=torch.bfloat16,
+                         kv_dtype=torch.bfloat16, scale=scale).float().cpu().numpy()
+    for got in folded + [per_query]:
+        np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    np.testing.assert_allclose(folded[0], per_query, atol=1e-2, rtol=0)
+    # queries before a sequence's first position see nothing
+    assert not folded[0][0, :max(0, tq - 2)].any()
+    assert ops.device_status(cuda_device.index or 0) == 0
+
+
+@pytest.mark.parametrize("kv", ["f16", "bf16_fp32q"])
+def test_prefill_page_once_other_types(cuda_device, kv):
+    """Folded queries on the f16-KV kernel (q split into f16 hi + lo, power-of-two
+    prescale) and with fp32 q over bf16 KV (hi + lo bf16 halves)."""
+    q, k, v, bt, ctx = _case([31, 700, 3000], 4, 32, 8, seed=81)
+    scale = 1 / math.sqrt(128)
+    if kv == "f16":
+        kr = k.astype(np.float16).astype(np.float32)
+        vr = v.astype(np.float16).astype(np.float32)
+        qr, q_dt, kv_dt = O.round_bf16(q), torch.bfloat16, torch.float16
+    else:
+        kr, vr = O.round_bf16(k), O.round_bf16(v)
+        qr, q_dt, kv_dt = q, torch.float32, torch.bfloat16
+    want = _oracle(qr, kr, vr, bt, ctx, scale, hkv=8, bs=16, causal=1)
+    got = _prefill(qr, kr, vr, bt, ctx, cuda_device, hkv=8, q_dtype=q_dt, kv_dtype=kv_dt,
+                   scale=scale).float().cpu().numpy()
+    np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
