@@ -482,7 +482,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 
     // bf16 q with bf16 KV: q's words are the score MMA's A fragments as they are, so the
     // next run's q can be loaded into registers while the current run merges.
-    constexpr bool kQPrefetch = std::is_same<KV, __nv_bfloat16>::value && !SPLIT;
+    constexpr bool kQPrefetch = std::is_same<KV, __nv_bfloat16>::value && !SPLIT && G <= 8;
     uint32_t qnext[kQPrefetch ? D / 16 : 1][2];
     bool have_qnext = false;
     int gidx = 0;        // CTA-local index of the run's first group
@@ -505,12 +505,17 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             // columns, so the probabilities go from the score accumulators straight
             // into the B operand.
             static_assert(ROWS == 16, "16-bit consumer: 16-token groups");
+            static_assert(G <= 16, "16-bit consumer: at most 16 rows");
+            // G = 16 (folded multi-query calls only): rows g + 8 are live too; their
+            // probabilities feed a second value MMA whose 8 columns are rows 8..15.
+            constexpr bool R2 = G > 8;
             constexpr int KS = D / 16;  // k-steps of the score MMA = m-tiles of the value MMA
             const int g = lane >> 2;    // fragment row group
             const int t = lane & 3;     // fragment column pair
             // q as A fragments (row g = head g; rows g+8 are zero), split hi + lo when the
             // input is wider than the MMA type so the scores stay fp32-accurate.
             uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
+            uint32_t qb[R2 ? KS : 1][2], qlb[(R2 && SPLIT) ? KS : 1][2];  // rows g + 8
             float qmul = a.q_scale;  // score multiplier (f16 KV: times the power of two taken out of q)
             if (kQPrefetch && have_qnext) {
 #pragma unroll
@@ -519,30 +524,35 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     qa[kk][1] = qnext[kk][1];
                 }
             } else {
-                const long long qrow = qo_row(r.s, r.h, g < G ? g : 0, Hkv, G, a.qfold, a.seq_div) * D;
-                float qx[KS][2][2];
+                constexpr int NH = R2 ? 2 : 1;  // row halves loaded: g, and g + 8 with 16 rows
+                float qx[NH][KS][2][2];
 #pragma unroll
-                for (int kk = 0; kk < KS; ++kk) {
+                for (int rh = 0; rh < NH; ++rh) {
+                    const int gr = g + 8 * rh;
+                    const long long qrow = qo_row(r.s, r.h, gr < G ? gr : 0, Hkv, G, a.qfold, a.seq_div) * D;
 #pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const int d = 16 * kk + 2 * t + 8 * hf;
-                        float x0 = 0.f, x1 = 0.f;
-                        if (g < G) {
-                            if (a.q_bf16) {
-                                const __nv_bfloat162 v2 =
-                                    *reinterpret_cast<const __nv_bfloat162 *>(
-                                        reinterpret_cast<const __nv_bfloat16 *>(a.q) + qrow + d);
-                                x0 = __low2float(v2);
-                                x1 = __high2float(v2);
-                            } else {
-                                const float2 v2 = *reinterpret_cast<const float2 *>(
-                                    reinterpret_cast<const float *>(a.q) + qrow + d);
-                                x0 = v2.x;
-                                x1 = v2.y;
+                    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+                        for (int hf = 0; hf < 2; ++hf) {
+                            const int d = 16 * kk + 2 * t + 8 * hf;
+                            float x0 = 0.f, x1 = 0.f;
+                            if (gr < G) {
+                                if (a.q_bf16) {
+                                    const __nv_bfloat162 v2 =
+                                        *reinterpret_cast<const __nv_bfloat162 *>(
+                                            reinterpret_cast<const __nv_bfloat16 *>(a.q) + qrow + d);
+                                    x0 = __low2float(v2);
+                                    x1 = __high2float(v2);
+                                } else {
+                                    const float2 v2 = *reinterpret_cast<const float2 *>(
+                                        reinterpret_cast<const float *>(a.q) + qrow + d);
+                                    x0 = v2.x;
+                                    x1 = v2.y;
+                                }
                             }
+                            qx[rh][kk][hf][0] = x0;
+                            qx[rh][kk][hf][1] = x1;
                         }
-                        qx[kk][hf][0] = x0;
-                        qx[kk][hf][1] = x1;
                     }
                 }
                 float down = 1.f;
@@ -551,10 +561,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     // back on the scores
                     float mx = 0.f;
 #pragma unroll
-                    for (int kk = 0; kk < KS; ++kk)
+                    for (int rh = 0; rh < NH; ++rh)
 #pragma unroll
-                        for (int hf = 0; hf < 2; ++hf)
-                            mx = fmaxf(mx, fmaxf(fabsf(qx[kk][hf][0]), fabsf(qx[kk][hf][1])));
+                        for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+                            for (int hf = 0; hf < 2; ++hf)
+                                mx = fmaxf(mx, fmaxf(fabsf(qx[rh][kk][hf][0]), fabsf(qx[rh][kk][hf][1])));
                     mx = warp_max(mx);
                     const int eq = mx >= 16384.f ? min(exp_of(mx) - 14, 126) : 0;
                     down = pow2i(-eq);
@@ -564,11 +576,19 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 for (int kk = 0; kk < KS; ++kk) {
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf) {
-                        const float x0 = qx[kk][hf][0] * down, x1 = qx[kk][hf][1] * down;
+                        const float x0 = qx[0][kk][hf][0] * down, x1 = qx[0][kk][hf][1] * down;
                         qa[kk][hf] = pack2<KV>(x0, x1);
                         if constexpr (SPLIT) {
                             const float2 back = unpack2<KV>(qa[kk][hf]);
                             ql[kk][hf] = pack2<KV>(x0 - back.x, x1 - back.y);
+                        }
+                        if constexpr (R2) {
+                            const float y0 = qx[NH - 1][kk][hf][0] * down, y1 = qx[NH - 1][kk][hf][1] * down;
+                            qb[kk][hf] = pack2<KV>(y0, y1);
+                            if constexpr (SPLIT) {
+                                const float2 back = unpack2<KV>(qb[kk][hf]);
+                                qlb[kk][hf] = pack2<KV>(y0 - back.x, y1 - back.y);
+                            }
                         }
                     }
                 }
@@ -576,11 +596,16 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float m_run = -INFINITY;  // running max of head g (quad-uniform)
             float l_run = 0.f;        // this lane's share of head g's normaliser
             float o[KS][4];           // O^T fragments: d = 16*mt + g (+8), heads 2t, 2t+1
+            float m_run2 = -INFINITY, l_run2 = 0.f;  // the same for row g + 8 (R2)
+            float o2[R2 ? KS : 1][4];                // heads 8 + 2t, 9 + 2t (R2)
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+#pragma unroll
+            for (int mt = 0; mt < (R2 ? KS : 1); ++mt) o2[mt][0] = o2[mt][1] = o2[mt][2] = o2[mt][3] = 0.f;
             // Folded multi-query rows: row g is query g / (G / qfold), which sees the
             // positions before len - qshift.
             const int qshift = (a.qfold > 1 && g < G) ? a.qfold - 1 - g / (G / a.qfold) : 0;
+            const int qshift2 = (R2 && a.qfold > 1) ? a.qfold - 1 - (g + 8) / (G / a.qfold) : 0;
             // ldmatrix row address of lane: token r + 8*(i>>1), 8 columns at 8*(i&1)
             const int lm_tok = (lane & 7) + 8 * (lane >> 4);
             const int lm_col = 8 * ((lane >> 3) & 1);
@@ -634,17 +659,20 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
                     float(*acc)[4] = (kk & 1) ? s2 : s;
-                    mma_16816<KV>(acc[0], qa[kk][0], 0u, qa[kk][1], 0u, kb[kk][0], kb[kk][1]);
-                    mma_16816<KV>(acc[1], qa[kk][0], 0u, qa[kk][1], 0u, kb[kk][2], kb[kk][3]);
+                    const uint32_t b0 = R2 ? qb[R2 ? kk : 0][0] : 0u, b1 = R2 ? qb[R2 ? kk : 0][1] : 0u;
+                    mma_16816<KV>(acc[0], qa[kk][0], b0, qa[kk][1], b1, kb[kk][0], kb[kk][1]);
+                    mma_16816<KV>(acc[1], qa[kk][0], b0, qa[kk][1], b1, kb[kk][2], kb[kk][3]);
                     if constexpr (SPLIT) {
-                        mma_16816<KV>(acc[0], ql[kk][0], 0u, ql[kk][1], 0u, kb[kk][0], kb[kk][1]);
-                        mma_16816<KV>(acc[1], ql[kk][0], 0u, ql[kk][1], 0u, kb[kk][2], kb[kk][3]);
+                        const uint32_t c0 = R2 ? qlb[(R2 && SPLIT) ? kk : 0][0] : 0u;
+                        const uint32_t c1 = R2 ? qlb[(R2 && SPLIT) ? kk : 0][1] : 0u;
+                        mma_16816<KV>(acc[0], ql[kk][0], c0, ql[kk][1], c1, kb[kk][0], kb[kk][1]);
+                        mma_16816<KV>(acc[1], ql[kk][0], c0, ql[kk][1], c1, kb[kk][2], kb[kk][3]);
                     }
                 }
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
+                    for (int e = 0; e < (R2 ? 4 : 2); ++e) s[nt][e] += s2[nt][e];
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
                 // (folded queries: row g's query sees qshift fewer positions than the last)
                 const int row_hi = min(v_hi, sw.len - qshift - t0);
@@ -698,7 +726,57 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt)
                     mma_16816<KV>(o[mt], vb[mt][0], vb[mt][1], vb[mt][2], vb[mt][3], pb0, pb1);
+                if constexpr (R2) {
+                    // ---------------- rows g + 8: the same softmax on accumulator entries
+                    // 2, 3, then the value MMA for columns (heads) 8..15
+                    const int row_hi2 = min(v_hi, sw.len - qshift2 - t0);
+                    float p2[2][2];
+                    float mloc2 = -INFINITY;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int tk = 8 * nt + 2 * t + e;
+                            float x2 = s[nt][2 + e] * qmul;
+                            if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
+                            x2 = (tk >= v_lo && tk < row_hi2) ? x2 : -INFINITY;
+                            p2[nt][e] = x2;
+                            mloc2 = fmaxf(mloc2, x2);
+                        }
+                    mloc2 = fmaxf(mloc2, __shfl_xor_sync(0xffffffffu, mloc2, 1));
+                    mloc2 = fmaxf(mloc2, __shfl_xor_sync(0xffffffffu, mloc2, 2));
+                    const float mn2 = fmaxf(m_run2, mloc2);
+                    const float alpha2 = (mn2 == m_run2) ? 1.f : fast_exp2(m_run2 - mn2);
+                    const float mref2 = (mn2 == -INFINITY) ? 0.f : mn2;
+                    m_run2 = mn2;
+                    float psum2 = 0.f;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            p2[nt][e] = fast_exp2(p2[nt][e] - mref2);
+                            psum2 += p2[nt][e];
+                        }
+                    l_run2 = l_run2 * alpha2 + psum2;
+                    const uint32_t pc0 = pack2<KV>(p2[0][0], p2[0][1]);
+                    const uint32_t pc1 = pack2<KV>(p2[1][0], p2[1][1]);
+                    if (__any_sync(0xffffffffu, alpha2 != 1.f)) {
+                        const float al0 = __shfl_sync(0xffffffffu, alpha2, 8 * t);      // head 8 + 2t
+                        const float al1 = __shfl_sync(0xffffffffu, alpha2, 8 * t + 4);  // head 9 + 2t
+#pragma unroll
+                        for (int mt = 0; mt < KS; ++mt) {
+                            o2[mt][0] *= al0;
+                            o2[mt][1] *= al1;
+                            o2[mt][2] *= al0;
+                            o2[mt][3] *= al1;
+                        }
+                    }
+#pragma unroll
+                    for (int mt = 0; mt < KS; ++mt)
+                        mma_16816<KV>(o2[mt], vb[mt][0], vb[mt][1], vb[mt][2], vb[mt][3], pc0, pc1);
+                }
             }
+
             gidx += r.len;
 
             // ---------------- next run's q, in flight while this run merges
@@ -723,6 +801,23 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 cw[g] = m_run;
                 cw[G + g] = l_run;
             }
+            if constexpr (R2) {
+                l_run2 += __shfl_xor_sync(0xffffffffu, l_run2, 1);
+                l_run2 += __shfl_xor_sync(0xffffffffu, l_run2, 2);
+                if (t == 0) {
+                    cw[g + 8] = m_run2;
+                    cw[G + g + 8] = l_run2;
+                }
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    const int d0 = 16 * mt + g;
+                    cw[2 * G + (8 + 2 * t) * D + d0] = o2[mt][0];
+                    cw[2 * G + (8 + 2 * t) * D + d0 + 8] = o2[mt][2];
+                    cw[2 * G + (9 + 2 * t) * D + d0] = o2[mt][1];
+                    cw[2 * G + (9 + 2 * t) * D + d0 + 8] = o2[mt][3];
+                }
+            }
+
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) {
                 const int d0 = 16 * mt + g;

@@ -246,7 +246,14 @@ const void *pick_fast(int kv, int D, int G, bool q_f32, int nc, int rows) {
         case GOLLEK_DTYPE_BF16:
             if (D == 128) {
                 if (nc == 8) return q_f32 ? pick_g<__nv_bfloat16, 128, 8, true>(G) : pick_g<__nv_bfloat16, 128, 8, false>(G);
-                if (nc == 7) return q_f32 ? pick_g<__nv_bfloat16, 128, 7, true>(G) : pick_g<__nv_bfloat16, 128, 7, false>(G);
+                if (nc == 7) {
+                    // 16 rows (folded multi-query calls): 7 consumer warps only, so that no
+                    // SM sub-partition holds three warps and a thread may use 255 registers
+                    if (G == 16)
+                        return q_f32 ? fast_kernel<__nv_bfloat16, 128, 16, 7, true, kRows>()
+                                     : fast_kernel<__nv_bfloat16, 128, 16, 7, false, kRows>();
+                    return q_f32 ? pick_g<__nv_bfloat16, 128, 7, true>(G) : pick_g<__nv_bfloat16, 128, 7, false>(G);
+                }
                 return nullptr;
             }
             if (D == 64 && nc == 8)
@@ -390,8 +397,12 @@ bool tma_layout_ok(const V2 &p, long long page_stride) {
 // warp count or nullptr.
 const void *fast_eligible(const V2 &p, int G, long long page_stride) {
     if (!tma_layout_ok(p, page_stride)) return nullptr;
+    if (G > 8 && p.qfold <= 1) return nullptr;  // 16-row kernels serve folded multi-query calls
     const NcList c = nc_candidates(p.kv_dtype, p.D);
-    return c.n ? pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c.v[0], group_rows(p)) : nullptr;
+    for (int i = 0; i < c.n; ++i)
+        if (const void *f = pick_fast(p.kv_dtype, p.D, G, p.q_dtype == GOLLEK_DTYPE_F32, c.v[i], group_rows(p)))
+            return f;
+    return nullptr;
 }
 
 // Split-K scratch: the caller's workspace, or the library's per (device, stream) one;
@@ -939,19 +950,22 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
     p.workspace_bytes = cap;
     // Page-once chunks: F queries of a sequence times its GQA group G as the rows of one
     // (sequence, kv-head) unit of the 16-bit mma.sync kernel (G*F one of its row counts
-    // 2, 4, 8), each row with its own causal limit, so a page is read once per F queries
-    // instead of once per query.  Causal, no sliding window (its start would differ per
-    // row), bf16/f16 KV.  F is the largest such divisor of Tq; GOLLEK_PREFILL_FOLD=0 keeps
-    // one query per decode sequence.  The partial slots need the same bytes either way.
+    // 2, 4, 8, and 16 for bf16 KV with head_dim 128), each row with its own causal limit,
+    // so a page is read once per F queries instead of once per query.  Causal, no sliding
+    // window (its start would differ per row), bf16/f16 KV.  F is the largest power of two
+    // dividing Tq whose rows have a compiled kernel; GOLLEK_PREFILL_FOLD=0 keeps one query
+    // per decode sequence.  The partial slots need the same bytes either way.
     const int G = num_q_heads / num_kv_heads;
-    int F = 1;
-    if (causal && sliding_window <= 0 && prefill_fold_enabled() &&
-        (kv_dtype == GOLLEK_DTYPE_BF16 || kv_dtype == GOLLEK_DTYPE_F16))
-        for (int f = 8 / std::max(G, 1); f > 1; f >>= 1)
-            if (num_queries % f == 0 && G * f <= 8) {
-                F = f;
-                break;
-            }
+    const bool foldable = causal && sliding_window <= 0 && prefill_fold_enabled() &&
+                          (kv_dtype == GOLLEK_DTYPE_BF16 || kv_dtype == GOLLEK_DTYPE_F16);
+    // rows of the 16-bit kernel: 16 for bf16 KV with head_dim 128, else 8
+    const int max_rows = (kv_dtype == GOLLEK_DTYPE_BF16 && head_dim == 128) ? 16 : 8;
+    auto next_fold = [&](int below) {
+        for (int f = below >> 1; f > 1; f >>= 1)
+            if (num_queries % f == 0 && G * f <= max_rows) return f;
+        return 1;
+    };
+    int F = foldable ? next_fold(2 * max_rows) : 1;
     for (;;) {
         const int C = num_queries / F;
         const long long nv = static_cast<long long>(num_seqs) * C;
@@ -966,7 +980,7 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
         rc = run_v2(p);
         if (rc != kNotTaken || F == 1) return rc;
         t_last_error.clear();
-        F = 1;  // the folded kernel was not available for this case: one query per sequence
+        F = next_fold(F);  // no kernel for these rows: fewer queries per pass (at last one)
     }
 }
 

@@ -119,10 +119,11 @@ def _prefill(q, k, v, bt, ctx, dev, *, hkv, q_dtype, kv_dtype, scale):
 
 
 @pytest.mark.parametrize("hq,hkv,tq", [(32, 8, 2), (32, 8, 4), (32, 8, 8), (8, 8, 8), (16, 8, 4),
-                                       (16, 8, 6), (64, 8, 2)])
+                                       (16, 8, 6), (64, 8, 2), (8, 8, 16), (16, 8, 8), (64, 8, 6)])
 def test_prefill_page_once_chunks(cuda_device, monkeypatch, hq, hkv, tq):
     """Causal bf16 multi-query calls whose queries fold into the decode kernel's rows
-    (F queries x G heads <= 8 per page read, F the largest power of two dividing Tq):
+    (F queries x G heads <= 16 per page read with head_dim 128, F the largest power of two
+    dividing Tq; 16 rows use the kernel's second value MMA):
     against the oracle, and against the same call with folding turned off
     (GOLLEK_PREFILL_FOLD=0: one decode sequence per query).  Lengths below Tq give queries
     that see nothing (zeros); 6000 tokens split across CTAs (split-K merge per row)."""
