@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload decode_bf16|decode_int8|decode_fp32|longctx|migrate|config1|
-                                prefill|cow] [--tq T]
+                                prefill|prefill_int8|cow] [--tq T]
 
 Default workload: Llama-3-8B-shaped bf16 decode attention, 32 query
 heads over 8 KV heads, head_dim 128, block 16, 64 sequences with context lengths
@@ -13,9 +13,9 @@ batch (sequences are independent units; no collective on the data path): weak sc
 Other workloads (run by hand, one JSON line each): decode_int8 (config 3), decode_fp32,
 longctx (config 5, KV heads sharded over the ranks, strong scaling), migrate (config 4,
 prefill ranks push KV blocks to decode ranks over NVLink), config1 (the legacy fp32
-symbol on config 1), prefill (multi-query causal attention, T query tokens per sequence
-over config 2's pool), cow (prompt-cache copy-on-write block copy inside one GPU's pool,
-config 4's block layout).
+symbol on config 1), prefill / prefill_int8 (multi-query causal attention, T query
+tokens per sequence over config 2's bf16 or config 3's int8 pool), cow (prompt-cache
+copy-on-write block copy inside one GPU's pool, config 4's block layout).
 
 --impl reference times the reference's own CPU algorithm for the same workload: the
 C restatement in oracle/ (the reference is Java; no JDK exists here), all host threads.
@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode_bf16",
                     choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate", "config1",
-                             "prefill", "cow"])
+                             "prefill", "prefill_int8", "cow"])
     ap.add_argument("--tq", type=int, default=4, help="prefill: query tokens per sequence")
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--gather", action="store_true", help="longctx: all-gather head-sharded outputs")
@@ -865,7 +865,8 @@ def bench_prefill(args, world, rank, local):
     from gollek_b200 import _lib, ops
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    batch = DecodeBatch("decode_bf16", args.seed + rank, dev)
+    int8 = args.workload == "prefill_int8"
+    batch = DecodeBatch("decode_int8" if int8 else "decode_bf16", args.seed + rank, dev)
     B, Hq, D = batch.q.shape
     Tq = args.tq
     g = torch.Generator(device=dev).manual_seed(args.seed + 11 + rank)
@@ -878,6 +879,8 @@ def bench_prefill(args, world, rank, local):
 
     def run(qd, od, bt, ctx):
         ops.paged_attention_prefill(qd, batch.k, batch.v, bt, ctx, num_kv_heads=batch.hkv,
+                                    k_scales=batch.k_scales, v_scales=batch.v_scales,
+                                    scale_strides=batch.scale_strides,
                                     block_size=batch.sh["bs"], num_blocks=batch.nb, causal=True,
                                     out=od, workspace=ws, stream=stream)
 
@@ -902,12 +905,13 @@ def bench_prefill(args, world, rank, local):
     h2d = sum(t.numel() * t.element_size() for t in (hq_, hbt, hctx))
     d2h = hout.numel() * hout.element_size()
 
-    # queries sharing one pass over the pages (the library's rule for causal bf16 calls
-    # with head_dim 128 and no window: F * G <= 16 rows; GOLLEK_PREFILL_FOLD=0 turns it off)
+    # queries sharing one pass over the pages (the library's rule for causal calls with
+    # head_dim 128 and no window: F * G <= 16 rows for bf16 KV, <= 8 for int8 KV;
+    # GOLLEK_PREFILL_FOLD=0 turns it off)
     G = Hq // batch.hkv
     fold = 1
     if os.environ.get("GOLLEK_PREFILL_FOLD", "1") != "0":
-        f = 16 // G
+        f = (8 if int8 else 16) // G
         while f > 1:
             if Tq % f == 0:
                 fold = f
@@ -930,15 +934,18 @@ def bench_prefill(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "query tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16 KV/q/out, f32 accumulate", "data": "synthetic (seeded; config 2 shapes)",
-            "config": {"workload": f"multi_query_causal_tq{Tq}_config2_pool", "batch_per_gpu": B,
+            "dtype": "int8 KV, bf16 q/out, f32 accumulate" if int8 else "bf16 KV/q/out, f32 accumulate",
+            "data": "synthetic (seeded; config 3 shapes)" if int8 else "synthetic (seeded; config 2 shapes)",
+            "config": {"workload": f"multi_query_causal_tq{Tq}_{'config3' if int8 else 'config2'}_pool",
+                       "batch_per_gpu": B,
                        "queries_per_seq": Tq, "queries_per_page_pass": fold, "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"],
                        "head_dim": sh["d"], "block_size": sh["bs"],
                        "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
                        "parallelism": f"independent batches x{world}",
                        "l2": f"no flush: {kv_once / 1e9:.2f} GB of KV per step per GPU > 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
-                         "frac": achieved_min / peak, "traffic": traffic_per_launch(f"prefill_tq{Tq}"),
+                         "frac": achieved_min / peak,
+                         "traffic": traffic_per_launch(f"prefill{'_int8' if int8 else ''}_tq{Tq}"),
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                          "algorithmic_bytes_per_launch": alg,
                          "note": "numerator counts each page once per step (page-once ideal); "
@@ -1137,7 +1144,7 @@ def main():
             bench_migrate(args, world, rank, local)
         elif args.workload == "config1":
             bench_config1(args, world, rank, local)
-        elif args.workload == "prefill":
+        elif args.workload in ("prefill", "prefill_int8"):
             bench_prefill(args, world, rank, local)
         elif args.workload == "cow":
             bench_cow(args, world, rank, local)

@@ -859,7 +859,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float qsum = 0.f;   // head g's sum of the f16 q values the MMAs see
             {
                 float qf[32];
-                const long long qrow = ((static_cast<long long>(r.s) * Hkv + r.h) * G + g) * D + 32 * t;
+                const long long qrow = qo_row(r.s, r.h, g < G ? g : 0, Hkv, G, a.qfold, a.seq_div) * D + 32 * t;
                 if (g < G) {
                     if (a.q_bf16) {
                         const uint4 *src = reinterpret_cast<const uint4 *>(
@@ -923,6 +923,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float m_run = -INFINITY;  // running max of head g (quad-uniform)
             float l_run = 0.f;        // this lane's share of head g's normaliser
             float ps_run = 0.f;       // this lane's share of head g's probability mass in o
+            // folded multi-query rows: row g's query sees the positions before len - qshift
+            const int qshift = (a.qfold > 1 && g < G) ? a.qfold - 1 - g / (G / a.qfold) : 0;
             int ev = 0;               // o holds O * 2^-ev
             bool ev_set = false;
             float o[KS][4];
@@ -1022,6 +1024,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) s[0][nt][e] -= qbias;
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
+                // (vmax spans the group's window, the same for every row, so the V-scale
+                // exponent stays warp-uniform; row g's own causal bound masks its scores)
+                const int row_hi = min(v_hi, sw.len - qshift - t0);
                 float p[NT][2];
                 bool valid[NT][2];
                 float mloc = -INFINITY;
@@ -1031,13 +1036,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int tk = 8 * nt + 2 * t + e;
-                        valid[nt][e] = tk >= v_lo && tk < v_hi;
+                        if (tk >= v_lo && tk < v_hi) vmax = fmaxf(vmax, vsc[nt][e]);
+                        valid[nt][e] = tk >= v_lo && tk < row_hi;
                         float x2 = s[0][nt][e] * qmul * ksc[nt][e];
                         if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
                         x2 = valid[nt][e] ? x2 : -INFINITY;
                         p[nt][e] = x2;
                         mloc = fmaxf(mloc, x2);
-                        if (valid[nt][e]) vmax = fmaxf(vmax, vsc[nt][e]);
                     }
                 mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
                 mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));

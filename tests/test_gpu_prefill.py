@@ -162,3 +162,49 @@ def test_prefill_page_once_other_types(cuda_device, kv):
     got = _prefill(qr, kr, vr, bt, ctx, cuda_device, hkv=8, q_dtype=q_dt, kv_dtype=kv_dt,
                    scale=scale).float().cpu().numpy()
     np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+
+
+@pytest.mark.parametrize("hq,tq,scales,qf32", [(32, 2, "token", False), (32, 4, "page", False),
+                                               (16, 4, "token", False), (8, 8, "page", False),
+                                               (32, 2, "token", True)])
+def test_prefill_page_once_int8(cuda_device, monkeypatch, hq, tq, scales, qf32):
+    """Causal multi-query calls over int8 KV fold F queries x G heads <= 8 rows into one
+    page pass of the int8 tensor-pipe kernel, with the reference's per-token scales or
+    one scale per (page, kv-head): against the oracle's INT8 restatement and against the
+    per-query form (GOLLEK_PREFILL_FOLD=0)."""
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([3, 20, 333, 1900, 5000], tq, hq, 8, seed=90 + tq + hq)
+    if scales == "token":
+        kq, ks = quantize_rows_int8(k)
+        vq, vs = quantize_rows_int8(v)
+        strides, ks_t, vs_t = (8 * 16, 16, 1), ks, vs
+    else:  # one scale per (page, kv-head): absmax over the page's rows / 127
+        def per_page(x):
+            amax = np.abs(x).max(axis=(2, 3))
+            sc = np.where(amax == 0, 1.0, amax / 127.0).astype(np.float32)
+            qq = np.clip(np.floor(x / sc[:, :, None, None] + 0.5), -127, 127).astype(np.int8)
+            return qq, sc
+        kq, ks_t = per_page(k)
+        vq, vs_t = per_page(v)
+        ks = np.repeat(ks_t[:, :, None], 16, axis=2)
+        vs = np.repeat(vs_t[:, :, None], 16, axis=2)
+        strides = (8, 1, 0)
+    qr = q if qf32 else O.round_bf16(q)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(qr, kq, vq, bt, ctx, scale, hkv=8, bs=16, causal=1, storage=O.INT8, ks=ks, vs=vs)
+
+    def call():
+        return ops.paged_attention_prefill(
+            _t(qr, cuda_device, torch.float32 if qf32 else torch.bfloat16), _t(kq, cuda_device),
+            _t(vq, cuda_device), _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=8,
+            block_size=16, scale=scale, num_blocks=k.shape[0], k_scales=_t(ks_t, cuda_device),
+            v_scales=_t(vs_t, cuda_device), scale_strides=strides).float().cpu().numpy()
+
+    folded = [call(), call()]
+    monkeypatch.setenv("GOLLEK_PREFILL_FOLD", "0")
+    per_query = call()
+    for got in folded + [per_query]:
+        np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    np.testing.assert_allclose(folded[0], per_query, atol=1e-2, rtol=0)
+    assert not folded[0][0, :max(0, tq - 3)].any()
+    assert ops.device_status(cuda_device.index or 0) == 0
