@@ -1151,9 +1151,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             {
                 const long long qbase = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
                 for (int i = tid; i < G * D; i += CONS) {
+                    // folded multi-query rows sit apart in q ([S, Tq, Hq, D])
+                    const long long qi = a.qfold > 1
+                                             ? qo_row(r.s, r.h, i / D, Hkv, G, a.qfold, a.seq_div) * D + (i % D)
+                                             : qbase + i;
                     const float v = a.q_bf16
-                                        ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.q)[qbase + i])
-                                        : reinterpret_cast<const float *>(a.q)[qbase + i];
+                                        ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(a.q)[qi])
+                                        : reinterpret_cast<const float *>(a.q)[qi];
                     sm_q[q_off(D, i / D, i % D)] = v * a.q_scale;
                 }
             }
@@ -1223,7 +1227,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         float x2 = dot[hh].x + dot[hh].y;
                         x2 += __shfl_xor_sync(0xffffffffu, x2, 16);
                         if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
-                        sc[hh] = valid ? x2 : -INFINITY;
+                        bool ok = valid;
+                        if (a.qfold > 1)  // folded row hh: its query sees the positions before len - qshift
+                            ok = ok && t0 + li < sw.len - (a.qfold - 1 - hh / (G / a.qfold));
+                        sc[hh] = ok ? x2 : -INFINITY;
                     }
                 }
 

@@ -949,16 +949,17 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
     p.workspace = ws;
     p.workspace_bytes = cap;
     // Page-once chunks: F queries of a sequence times its GQA group G as the rows of one
-    // (sequence, kv-head) unit of the tensor-pipe decode kernel (G*F one of its row counts
+    // (sequence, kv-head) unit of the decode kernel (G*F one of its row counts
     // 2, 4, 8, and 16 for bf16 KV with head_dim 128), each row with its own causal limit,
     // so a page is read once per F queries instead of once per query.  Causal, no sliding
-    // window (its start would differ per row), bf16/f16 KV or int8 KV with head_dim 128.
+    // window (its start would differ per row), bf16/f16/fp32 KV or int8 KV with head_dim 128.
     // F is the largest power of two dividing Tq whose rows have a compiled kernel;
     // GOLLEK_PREFILL_FOLD=0 keeps one query per decode sequence.  The partial slots need
     // the same bytes either way.
     const int G = num_q_heads / num_kv_heads;
     const bool foldable = causal && sliding_window <= 0 && prefill_fold_enabled() &&
                           (kv_dtype == GOLLEK_DTYPE_BF16 || kv_dtype == GOLLEK_DTYPE_F16 ||
+                           kv_dtype == GOLLEK_DTYPE_F32 ||
                            (kv_dtype == GOLLEK_DTYPE_I8 && head_dim == 128));
     // rows of the kernel: 16 for bf16 KV with head_dim 128, else 8
     const int max_rows = (kv_dtype == GOLLEK_DTYPE_BF16 && head_dim == 128) ? 16 : 8;

@@ -208,3 +208,31 @@ def test_prefill_page_once_int8(cuda_device, monkeypatch, hq, tq, scales, qf32):
     np.testing.assert_allclose(folded[0], per_query, atol=1e-2, rtol=0)
     assert not folded[0][0, :max(0, tq - 3)].any()
     assert ops.device_status(cuda_device.index or 0) == 0
+
+
+@pytest.mark.parametrize("hq,hkv,d,tq", [(8, 8, 64, 8), (32, 8, 128, 2), (16, 8, 128, 4)])
+def test_prefill_page_once_fp32(cuda_device, monkeypatch, hq, hkv, d, tq):
+    """Causal multi-query calls over the reference's own fp32 KV storage fold F queries x
+    G heads <= 8 rows into one page pass of the CUDA-core fp32 kernel: within 1e-4 of the
+    output scale against the oracle, with folding and without (GOLLEK_PREFILL_FOLD=0)."""
+    from gollek_b200 import ops
+    qd, k, v, bt, ctx = decode_case([4, 37, 301, 512, 3000], hq=hq, hkv=hkv, d=d, bs=16,
+                                    seed=110 + tq + hq, kv_std=1.0)
+    q = np.random.default_rng(111 + tq).standard_normal((len(ctx), tq, hq, d)).astype(np.float32)
+    scale = 1 / math.sqrt(d)
+    want = _oracle(q, k, v, bt, ctx, scale, hkv=hkv, bs=16, causal=1)
+
+    def call():
+        return ops.paged_attention_prefill(_t(q, cuda_device), _t(k, cuda_device), _t(v, cuda_device),
+                                           _t(bt, cuda_device), _t(ctx, cuda_device), num_kv_heads=hkv,
+                                           block_size=16, scale=scale,
+                                           num_blocks=k.shape[0]).cpu().numpy()
+
+    folded = [call(), call()]
+    monkeypatch.setenv("GOLLEK_PREFILL_FOLD", "0")
+    per_query = call()
+    tol = 1e-4 * max(1.0, float(np.abs(want).max()))
+    for got in folded + [per_query]:
+        assert np.abs(got - want).max() <= tol
+    assert not folded[0][0, :max(0, tq - 4)].any()
+    assert ops.device_status(cuda_device.index or 0) == 0
