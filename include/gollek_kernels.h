@@ -153,8 +153,8 @@ GOLLEK_API size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_
  *   sliding_window  > 0: the last sliding_window positions up to the query (causal only
  *                 when num_queries > 1; otherwise GOLLEK_ERR_UNSUPPORTED)
  *   workspace     >= gollek_paged_attention_prefill_workspace_size(...), or NULL
- * Every other argument as gollek_paged_attention_v2.  Causal calls over bf16/f16 KV, or
- * int8 KV with head_dim 128, without a window read each page once per F queries: F (the
+ * Every other argument as gollek_paged_attention_v2.  Causal calls over bf16/f16/fp32 KV,
+ * or int8 KV with head_dim 128, without a window read each page once per F queries: F (the
  * largest power of two that divides num_queries with F * num_q_heads / num_kv_heads <= 16
  * for bf16 KV with head_dim 128, <= 8 otherwise) queries of a sequence share one pass over its pages as
  * extra rows of the decode kernel, each row with its own causal bound.  Other calls read
