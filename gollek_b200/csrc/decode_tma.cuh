@@ -1227,10 +1227,13 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         float x2 = dot[hh].x + dot[hh].y;
                         x2 += __shfl_xor_sync(0xffffffffu, x2, 16);
                         if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
-                        bool ok = valid;
-                        if (a.qfold > 1)  // folded row hh: its query sees the positions before len - qshift
-                            ok = ok && t0 + li < sw.len - (a.qfold - 1 - hh / (G / a.qfold));
-                        sc[hh] = ok ? x2 : -INFINITY;
+                        sc[hh] = valid ? x2 : -INFINITY;
+                    }
+                    if (a.qfold > 1) {  // folded row hh: its query sees the positions before len - qshift
+                        const int gm = G / a.qfold;
+    #pragma unroll
+                        for (int hh = 0; hh < G; ++hh)
+                            if (t0 + li >= sw.len - (a.qfold - 1 - hh / gm)) sc[hh] = -INFINITY;
                     }
                 }
 
