@@ -54,9 +54,9 @@ SIGNATURES = {
     "gollek_kv_append": (_c_int, [_vp, _vp, _c_int, _vp, _vp, _vp, _c_int, _c_int, _vp, _vp, _vp,
                                   _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_ll, _c_ll, _c_ll,
                                   _c_ll, _vp]),
-    "gollek_kv_migrate": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_ll, _c_ll, _c_ll,
-                                   _c_int, _vp]),
-    "gollek_kv_block_checksum": (_c_int, [_vp, _vp, _c_int, _c_ll, _c_ll, _vp, _vp]),
+    "gollek_kv_migrate": (_c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll,
+                                   _c_ll, _c_ll, _c_int, _vp]),
+    "gollek_kv_block_checksum": (_c_int, [_vp, _vp, _c_int, _c_int, _c_ll, _c_ll, _vp, _vp]),
     "gollek_enable_peer_access": (_c_int, [_c_int, _c_int]),
     "gollek_ipc_get_handle": (_c_int, [_vp, _vp, ctypes.POINTER(_c_ll)]),
     "gollek_ipc_open_handle": (_c_int, [_vp, ctypes.POINTER(_vp)]),

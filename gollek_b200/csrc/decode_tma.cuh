@@ -1345,7 +1345,28 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             }
         }
         named_barrier(1, CONS);
-        if (*cons_abort) break;  // a wait gave up in this CTA: stop cleanly
+        if (*cons_abort) {
+            // A wait gave up in this CTA: stop cleanly, but let every split-K piece this
+            // CTA still owns (this run and the rest of its range) arrive on its counter,
+            // so that whoever arrives last resets the counter and the scratch is zeroed
+            // for the next call.  The last arriver merges whatever partials it finds; the
+            // call's result is void anyway (GOLLEK_STATUS_TIMEOUT is raised).
+            if (tid == 0) {
+                auto arrive_only = [&](const Run &rr) {
+                    if (rr.pieces <= 1) return;
+                    int *c = &a.counters[rr.s * Hkv + rr.h];
+                    if (atomicAdd(c, 1) == rr.pieces - 1) atomicExch(c, 0);
+                };
+                arrive_only(r);
+                for (long long y = x; y < x_end;) {
+                    Run rn = run_at(y);
+                    run_pieces(rn);
+                    y += rn.len;
+                    arrive_only(rn);
+                }
+            }
+            break;
+        }
 
         const long long out_row = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
         // element o of the (s, h) state [G][D] in out (folded queries: [S, qfold, Hq, D])

@@ -698,6 +698,19 @@ int check_v2(const V2 &p) {
     return GOLLEK_OK;
 }
 
+// After a wait gave up (GOLLEK_STATUS_TIMEOUT) a split-K arrival counter may have been
+// left non-zero; zero the counter regions of this device's library-owned workspaces.
+// Called with the device current and idle (after a synchronize).
+int rezero_library_counters(int dev) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto &kv : g_ws) {
+        if (std::get<0>(kv.first) != dev || !kv.second.first) continue;
+        GK_CUDA(cudaMemset(kv.second.first, 0, ws_counter_region(kv.second.second)),
+                "cudaMemset(split-K counters after a timeout)");
+    }
+    return GOLLEK_OK;
+}
+
 int read_and_clear_status(cudaStream_t st, unsigned *out) {
     unsigned v = 0;
     GK_CUDA(cudaMemcpyFromSymbolAsync(&v, g_status, sizeof(v), 0, cudaMemcpyDeviceToHost, st),
@@ -708,6 +721,13 @@ int read_and_clear_status(cudaStream_t st, unsigned *out) {
         GK_CUDA(cudaMemcpyToSymbolAsync(g_status, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice, st),
                 "clear status");
         GK_CUDA(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    }
+    if (v & GOLLEK_STATUS_TIMEOUT) {
+        int dev = 0;
+        GK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+        GK_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        const int rc = rezero_library_counters(dev);
+        if (rc) return rc;
     }
     *out = v;
     return GOLLEK_OK;
@@ -726,7 +746,10 @@ int status_to_code(unsigned v) {
 
 // Split-K scratch of gollek_paged_attention_v2_noalloc: a static device array, so that
 // entry point never allocates.  Host code cannot use the array's name as a device
-// address; noalloc_scratch() looks the address up per device (with it current).
+// address; noalloc_scratch() looks the address up per device (with it current) and
+// caches it for the life of the process.  The cached address belongs to the device's
+// primary context: after cudaDeviceReset (which destroys that context) it is stale, so a
+// process that resets a device must not call the no-alloc entry point on it again.
 __device__ __align__(256) unsigned char g_noalloc_scratch[GOLLEK_NOALLOC_SCRATCH_BYTES];
 
 std::mutex g_na_mu;
@@ -1069,6 +1092,15 @@ int gollek_kv_append(const void *key, const void *value, int src_dtype, const in
                                          : static_cast<long long>(num_kv_heads) * block_size * head_dim;
     if (kv_dtype == GOLLEK_DTYPE_I4 && ((head_dim & 1) || (ps & 1)))
         return fail(GOLLEK_ERR_UNSUPPORTED, "int4 pools need an even head_dim and page stride");
+    // The append quantises each row with its own absmax (the reference's per-token scale,
+    // PagedKvCacheQuantization.java:66-80).  With scale_token_stride == 0 every row of a
+    // page would overwrite the page's one shared scale and silently rescale the rows
+    // written before it (rows of one launch would also race on that slot).
+    if ((kv_dtype == GOLLEK_DTYPE_I8 || kv_dtype == GOLLEK_DTYPE_I4) && (k_scales || v_scales) &&
+        scale_token_stride == 0)
+        return fail(GOLLEK_ERR_UNSUPPORTED,
+                    "appending to an int8/int4 pool needs per-token scales (scale_token_stride != 0); "
+                    "a scale shared by a page's rows cannot take rows one at a time");
     if (num_tokens == 0) return GOLLEK_OK;
     AppendArgs a;
     a.key = key;
@@ -1100,15 +1132,21 @@ int gollek_kv_append(const void *key, const void *value, int src_dtype, const in
 
 int gollek_kv_migrate(const void *src_k, const void *src_v, void *dst_k, void *dst_v,
                       const int *src_blocks, const int *dst_blocks, int num_copies,
-                      long long src_block_stride, long long dst_block_stride, long long bytes_per_block,
-                      int device, void *stream) {
+                      int src_num_blocks, int dst_num_blocks, long long src_block_stride,
+                      long long dst_block_stride, long long bytes_per_block, int device,
+                      void *stream) {
     t_last_error.clear();
     if (!src_k || !dst_k || !src_blocks || !dst_blocks)
         return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
     if ((src_v == nullptr) != (dst_v == nullptr))
         return fail(GOLLEK_ERR_INVALID_ARGUMENT, "src_v and dst_v must both be set or both NULL");
-    if (num_copies < 0 || bytes_per_block < 0 || src_block_stride < 0 || dst_block_stride < 0)
+    if (num_copies < 0 || bytes_per_block < 0 || src_block_stride < 0 || dst_block_stride < 0 ||
+        src_num_blocks < 0 || dst_num_blocks < 0)
         return fail(GOLLEK_ERR_INVALID_ARGUMENT, "negative size");
+    if ((src_num_blocks > 0 && bytes_per_block > src_block_stride) ||
+        (dst_num_blocks > 0 && bytes_per_block > dst_block_stride))
+        return fail(GOLLEK_ERR_INVALID_ARGUMENT,
+                    "bytes_per_block %lld exceeds a block stride of a bounded pool", bytes_per_block);
     if (num_copies == 0 || bytes_per_block == 0) return GOLLEK_OK;
     DeviceGuard guard(device);
     MigrateArgs a;
@@ -1122,6 +1160,8 @@ int gollek_kv_migrate(const void *src_k, const void *src_v, void *dst_k, void *d
     a.dst_stride = dst_block_stride;
     a.bytes = bytes_per_block;
     a.tensors = src_v ? 2 : 1;
+    a.src_num_blocks = src_num_blocks;
+    a.dst_num_blocks = dst_num_blocks;
     a.segs_per_block = (bytes_per_block + kSegBytes - 1) / kSegBytes;
     a.num_units = static_cast<long long>(num_copies) * a.tensors * a.segs_per_block;
     const bool vec = aligned16(src_k) && aligned16(dst_k) && (!src_v || (aligned16(src_v) && aligned16(dst_v))) &&
@@ -1136,15 +1176,18 @@ int gollek_kv_migrate(const void *src_k, const void *src_v, void *dst_k, void *d
     return GOLLEK_OK;
 }
 
-int gollek_kv_block_checksum(const void *pool, const int *blocks, int n, long long block_stride,
-                             long long bytes_per_block, unsigned long long *checksums, void *stream) {
+int gollek_kv_block_checksum(const void *pool, const int *blocks, int n, int num_blocks,
+                             long long block_stride, long long bytes_per_block,
+                             unsigned long long *checksums, void *stream) {
     t_last_error.clear();
     if (!pool || !blocks || !checksums) return fail(GOLLEK_ERR_INVALID_ARGUMENT, "null pointer");
-    if (n < 0 || bytes_per_block % 8 != 0 || (reinterpret_cast<uintptr_t>(pool) & 7u) || block_stride % 8)
+    if (n < 0 || num_blocks < 0 || bytes_per_block % 8 != 0 ||
+        (reinterpret_cast<uintptr_t>(pool) & 7u) || block_stride % 8)
         return fail(GOLLEK_ERR_INVALID_ARGUMENT, "checksums need 8-byte aligned blocks");
     if (n == 0) return GOLLEK_OK;
     block_checksum_kernel<<<n, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint8_t *>(pool), blocks, block_stride, bytes_per_block, checksums);
+        static_cast<const uint8_t *>(pool), blocks, num_blocks, block_stride, bytes_per_block,
+        checksums);
     GK_CUDA(cudaGetLastError(), "block_checksum_kernel launch");
     return GOLLEK_OK;
 }
@@ -1210,6 +1253,10 @@ int gollek_device_status(int device, int clear, unsigned int *status_out) {
     if (clear) {
         const unsigned zero = 0;
         GK_CUDA(cudaMemcpyToSymbol(g_status, &zero, sizeof(zero)), "clear status");
+    }
+    if (v & GOLLEK_STATUS_TIMEOUT) {
+        const int rc = rezero_library_counters(device);
+        if (rc) return rc;
     }
     *status_out = v;
     return GOLLEK_OK;

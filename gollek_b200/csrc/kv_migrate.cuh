@@ -5,6 +5,9 @@
 // still spread over every SM.  A thread moves 4 x 16 bytes per step: four
 // independent loads from local HBM in flight, then four 16-byte stores, which go
 // over NVLink when the destination is a peer's memory.  Plain loads and stores only.
+// Block ids outside a pool's [0, num_blocks) (when the caller gives num_blocks) are
+// skipped and raise GOLLEK_STATUS_BAD_BLOCK_ID, so a stale or sentinel id never turns
+// into a store outside the destination pool, a peer's included.
 #pragma once
 
 #include "common.cuh"
@@ -22,7 +25,19 @@ struct MigrateArgs {
     long long segs_per_block;
     long long num_units;  // num_copies * tensors * segs_per_block
     int tensors;
+    int src_num_blocks, dst_num_blocks;  // 0: unchecked
 };
+
+// True when both ids of copy i lie inside their pools (every thread of the CTA reads
+// the same ids, so the test is uniform across the CTA).
+__device__ __forceinline__ bool migrate_ids_ok(const MigrateArgs &a, long long i, int &s, int &d) {
+    s = a.src_blocks[i];
+    d = a.dst_blocks[i];
+    const bool ok = s >= 0 && d >= 0 && (a.src_num_blocks <= 0 || s < a.src_num_blocks) &&
+                    (a.dst_num_blocks <= 0 || d < a.dst_num_blocks);
+    if (!ok && threadIdx.x == 0) raise_status(GOLLEK_STATUS_BAD_BLOCK_ID);
+    return ok;
+}
 
 __global__ void __launch_bounds__(512) kv_migrate_kernel_v16(const MigrateArgs a) {
     for (long long u = blockIdx.x; u < a.num_units; u += gridDim.x) {
@@ -30,10 +45,12 @@ __global__ void __launch_bounds__(512) kv_migrate_kernel_v16(const MigrateArgs a
         const long long bt = u / a.segs_per_block;
         const int tensor = static_cast<int>(bt % a.tensors);
         const long long i = bt / a.tensors;
+        int sb, db;
+        if (!migrate_ids_ok(a, i, sb, db)) continue;
         const uint4 *src = reinterpret_cast<const uint4 *>(
-            a.src[tensor] + static_cast<long long>(a.src_blocks[i]) * a.src_stride + seg * kSegBytes);
+            a.src[tensor] + static_cast<long long>(sb) * a.src_stride + seg * kSegBytes);
         uint4 *dst = reinterpret_cast<uint4 *>(
-            a.dst[tensor] + static_cast<long long>(a.dst_blocks[i]) * a.dst_stride + seg * kSegBytes);
+            a.dst[tensor] + static_cast<long long>(db) * a.dst_stride + seg * kSegBytes);
         const long long rem = a.bytes - seg * kSegBytes;
         const int n16 = static_cast<int>((rem < kSegBytes ? rem : kSegBytes) >> 4);
         int k = threadIdx.x;
@@ -58,23 +75,32 @@ __global__ void __launch_bounds__(256) kv_migrate_kernel_bytes(const MigrateArgs
         const long long bt = u / a.segs_per_block;
         const int tensor = static_cast<int>(bt % a.tensors);
         const long long i = bt / a.tensors;
-        const uint8_t *src = a.src[tensor] + static_cast<long long>(a.src_blocks[i]) * a.src_stride +
-                             seg * kSegBytes;
-        uint8_t *dst = a.dst[tensor] + static_cast<long long>(a.dst_blocks[i]) * a.dst_stride +
-                       seg * kSegBytes;
+        int sb, db;
+        if (!migrate_ids_ok(a, i, sb, db)) continue;
+        const uint8_t *src = a.src[tensor] + static_cast<long long>(sb) * a.src_stride + seg * kSegBytes;
+        uint8_t *dst = a.dst[tensor] + static_cast<long long>(db) * a.dst_stride + seg * kSegBytes;
         const long long rem = a.bytes - seg * kSegBytes;
         const long long n = rem < kSegBytes ? rem : kSegBytes;
         for (long long k = threadIdx.x; k < n; k += blockDim.x) dst[k] = src[k];
     }
 }
 
-// One CTA per block: sum over 8-byte words w_j of (w_j ^ (j * golden)) mod 2^64.
+// One CTA per block: sum over 8-byte words w_j of (w_j ^ (j * golden)) mod 2^64.  An id
+// outside [0, num_blocks) (num_blocks > 0) reads nothing, gets checksum 0 and raises
+// GOLLEK_STATUS_BAD_BLOCK_ID.
 __global__ void __launch_bounds__(256) block_checksum_kernel(const uint8_t *pool, const int *blocks,
-                                                             long long stride, long long bytes,
-                                                             unsigned long long *out) {
+                                                             int num_blocks, long long stride,
+                                                             long long bytes, unsigned long long *out) {
     __shared__ unsigned long long part[8];
-    const uint64_t *w =
-        reinterpret_cast<const uint64_t *>(pool + static_cast<long long>(blocks[blockIdx.x]) * stride);
+    const int b = blocks[blockIdx.x];
+    if (b < 0 || (num_blocks > 0 && b >= num_blocks)) {
+        if (threadIdx.x == 0) {
+            raise_status(GOLLEK_STATUS_BAD_BLOCK_ID);
+            out[blockIdx.x] = 0;
+        }
+        return;
+    }
+    const uint64_t *w = reinterpret_cast<const uint64_t *>(pool + static_cast<long long>(b) * stride);
     const long long n = bytes >> 3;
     unsigned long long acc = 0;
     for (long long j = threadIdx.x; j < n; j += blockDim.x)

@@ -131,29 +131,51 @@ def kv_append(key, value, token_pos, block_tables, k_cache, v_cache, *, block_si
     check(rc)
 
 
+def pool_blocks(pool, block_stride, bytes_per_block) -> int:
+    """Whole blocks of `bytes_per_block` bytes, `block_stride` bytes apart, that fit in
+    the tensor `pool` (the bound the migration and checksum kernels check ids against)."""
+    nbytes = pool.numel() * pool.element_size()
+    if nbytes < bytes_per_block or block_stride <= 0:
+        return 0 if block_stride <= 0 else -1
+    return (nbytes - bytes_per_block) // block_stride + 1
+
+
 def kv_migrate(src_k, src_v, dst_k, dst_v, src_blocks, dst_blocks, *, src_block_stride,
                dst_block_stride, bytes_per_block, device=None, stream=None, dst_k_ptr=None,
-               dst_v_ptr=None):
+               dst_v_ptr=None, src_num_blocks=None, dst_num_blocks=None):
     """Block-remapped copy (gollek_kv_migrate).  Strides/sizes in bytes.
 
     dst_k_ptr/dst_v_ptr override the destination with raw device addresses (a peer
-    pointer mapped through CUDA IPC)."""
+    pointer mapped through CUDA IPC); give dst_num_blocks with them.  Pool sizes default
+    to what the tensors hold, so ids outside a pool are skipped on the device and
+    reported by device_status() (GOLLEK_STATUS_BAD_BLOCK_ID)."""
     dev = src_k.device.index if device is None else device
     dk = dst_k_ptr if dst_k_ptr is not None else _ptr(dst_k)
     dv = dst_v_ptr if dst_v_ptr is not None else _ptr(dst_v)
+    if src_num_blocks is None:
+        src_num_blocks = pool_blocks(src_k, src_block_stride, bytes_per_block)
+    if dst_num_blocks is None:
+        dst_num_blocks = (pool_blocks(dst_k, dst_block_stride, bytes_per_block)
+                          if dst_k_ptr is None else 0)
+    if src_num_blocks < 0 or dst_num_blocks < 0:
+        raise ValueError("a pool tensor is smaller than one block")
     rc = _lib.load().gollek_kv_migrate(
         _ptr(src_k), _ptr(src_v), dk, dv, _ptr(src_blocks), _ptr(dst_blocks), src_blocks.numel(),
-        int(src_block_stride), int(dst_block_stride), int(bytes_per_block), int(dev),
-        _stream(src_k, stream))
+        int(src_num_blocks), int(dst_num_blocks), int(src_block_stride), int(dst_block_stride),
+        int(bytes_per_block), int(dev), _stream(src_k, stream))
     check(rc)
 
 
-def block_checksums(pool, blocks, *, block_stride, bytes_per_block, stream=None):
+def block_checksums(pool, blocks, *, block_stride, bytes_per_block, num_blocks=None, stream=None):
     """Per-block 64-bit checksums (gollek_kv_block_checksum) as an int64 tensor."""
+    if num_blocks is None:
+        num_blocks = pool_blocks(pool, block_stride, bytes_per_block)
+    if num_blocks < 0:
+        raise ValueError("the pool tensor is smaller than one block")
     out = torch.empty(blocks.numel(), dtype=torch.int64, device=pool.device)
     rc = _lib.load().gollek_kv_block_checksum(_ptr(pool), _ptr(blocks), blocks.numel(),
-                                              int(block_stride), int(bytes_per_block), _ptr(out),
-                                              _stream(pool, stream))
+                                              int(num_blocks), int(block_stride),
+                                              int(bytes_per_block), _ptr(out), _stream(pool, stream))
     check(rc)
     return out
 

@@ -61,8 +61,8 @@ class PrefillDecodeDisaggService:
 
     # ---- transfer (:401-435)
     def transfer_kv_to_decode_partition(self, request_id: str, prefill_blocks, kv_transfer_id: str,
-                                        dst_pool=None, dst_device: int | None = None,
-                                        decode_blocks=None, stream=None) -> list[int]:
+                                        dst_pool=None, decode_blocks=None,
+                                        stream=None) -> list[int]:
         """Copy every layer's K and V of prefill_blocks[i] to decode_blocks[i].
 
         dst_pool: (k, v) device tensors of another device's pool with this pool's layout;
@@ -86,8 +86,8 @@ class PrefillDecodeDisaggService:
         s = torch.tensor(list(prefill_blocks), dtype=torch.int32, device=dev)
         d = torch.tensor(list(decode_blocks), dtype=torch.int32, device=dev)
         ops.kv_migrate(src_k, src_v, dk, dv, s, d, src_block_stride=per_block,
-                       dst_block_stride=per_block, bytes_per_block=per_block,
-                       device=dev.index if dst_device is None else dev.index, stream=stream)
+                       dst_block_stride=per_block, bytes_per_block=per_block, device=dev.index,
+                       stream=stream)
         copied = 2 * per_block * len(prefill_blocks)
         self.total_kv_transfers += 1
         self.kv_transfer_bytes_total += copied

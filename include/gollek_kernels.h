@@ -122,8 +122,12 @@ GOLLEK_API int gollek_cuda_device_name(char *buf, int len);
  *   num_blocks pool size in pages, for device-side bounds checks (0: unchecked).
  *   scale      softmax scale; soft_cap > 0 applies cap*tanh(score/cap).
  *   workspace  split-K scratch of at least gollek_paged_attention_workspace_size(...)
- *              bytes, zero-filled before its first use and left zeroed by every call;
- *              NULL = library-owned scratch cached per (device, stream).
+ *              bytes, zero-filled before its first use and left zeroed by every call
+ *              that completes; NULL = library-owned scratch cached per (device, stream).
+ *              After a call whose device wait gave up (GOLLEK_STATUS_TIMEOUT from
+ *              gollek_device_status, GOLLEK_ERR_TIMEOUT from a synchronous call) the
+ *              caller must zero its workspace again before reusing it; the library
+ *              re-zeroes its own scratch when it reports the timeout.
  * Asynchronous on `stream`.  Numerics: fp32 scores, softmax and accumulation.
  */
 GOLLEK_API int gollek_paged_attention_v2(void *out, const void *q, const void *k_cache, const void *v_cache,
@@ -189,7 +193,9 @@ GOLLEK_API size_t gollek_paged_attention_prefill_workspace_size(int num_seqs, in
  *   - Calls whose gollek_paged_attention_workspace_size(...) exceeds that size are
  *     rejected with GOLLEK_ERR_WORKSPACE; nothing is launched.
  *   - The first call on a device looks up the array's device address (with that device
- *     current) and caches it; make that first call before any stream capture.
+ *     current) and caches it; make that first call before any stream capture.  The
+ *     cached address lives as long as the device's primary context: do not call this
+ *     entry point on a device after cudaDeviceReset in the same process.
  *   - Each call clears the scratch's arrival counters on `stream` before the kernel and
  *     never calls cudaMalloc, cudaFree or any allocating routine.
  *   - All calls on a device share the one array: calls that overlap on the GPU (on
@@ -222,7 +228,11 @@ GOLLEK_API int gollek_paged_attention_v2_noalloc(
  *   F32/BF16/F16 pools store the (converted) values.  I8 (I4) pools store
  *   clamp(Math.round(x/s), -127, 127) (clamp(.., -8, 7)) with s = absmax/127 (absmax/7)
  *   over the row, s = 1 for an all-zero row, and write s to the scale slot -- bit for
- *   bit what the reference's Java computes.  I4 needs an even head_dim.
+ *   bit what the reference's Java computes.  I4 needs an even head_dim.  I8/I4 pools
+ *   need per-token scales (scale_token_stride != 0): with a scale shared by a page's
+ *   rows (scale_token_stride == 0) each appended row would overwrite the shared scale
+ *   and rescale the rows already in the page, so such calls return
+ *   GOLLEK_ERR_UNSUPPORTED.  (Decode reads either granularity.)
  * Asynchronous on `stream`.
  */
 GOLLEK_API int gollek_kv_append(const void *key, const void *value, int src_dtype, const int *token_seq,
@@ -247,7 +257,12 @@ GOLLEK_API int gollek_kv_append(const void *key, const void *value, int src_dtyp
  *   src_k + src_blocks[i]*src_block_stride  ->  dst_k + dst_blocks[i]*dst_block_stride
  * and the same for V (src_v/dst_v may be NULL to copy K only).  src_blocks/dst_blocks
  * are device int32 arrays on the device the kernel runs on, `device`, which must also
- * hold the source pools.  The destination may be this device's memory (the reference's
+ * hold the source pools.  src_num_blocks / dst_num_blocks are the pools' sizes in
+ * blocks (0 = unchecked): a copy whose source or destination id lies outside
+ * [0, num_blocks) -- or is negative, whatever the size -- is skipped and raises
+ * GOLLEK_STATUS_BAD_BLOCK_ID (read it with gollek_device_status), as
+ * PhysicalBlockPool.getKBlock rejects such ids (KV/PhysicalBlockPool.java:147-159).  A
+ * bounded pool needs bytes_per_block <= its block stride.  The destination may be this device's memory (the reference's
  * two partitions of one pool; also the prompt cache's copy-on-write) or a peer's:
  * a peer pointer after gollek_enable_peer_access(device, peer) or one mapped with
  * gollek_ipc_open_handle().  The kernel reads locally and stores over NVLink with
@@ -255,18 +270,21 @@ GOLLEK_API int gollek_kv_append(const void *key, const void *value, int src_dtyp
  */
 GOLLEK_API int gollek_kv_migrate(const void *src_k, const void *src_v, void *dst_k, void *dst_v,
                       const int *src_blocks, const int *dst_blocks, int num_copies,
-                      long long src_block_stride, long long dst_block_stride,
-                      long long bytes_per_block, int device, void *stream);
+                      int src_num_blocks, int dst_num_blocks, long long src_block_stride,
+                      long long dst_block_stride, long long bytes_per_block, int device,
+                      void *stream);
 
 /*
  * Per-block 64-bit checksums, sum over the block's 8-byte words w_j of
  * (w_j XOR (j * 0x9E3779B97F4A7C15)) mod 2^64, of pool + blocks[i]*block_stride for
  * i < n (bytes_per_block a multiple of 8).  Lets a caller verify a migration of any
- * size without moving the blocks back to the host.  Asynchronous on `stream`.
+ * size without moving the blocks back to the host.  num_blocks is the pool's size in
+ * blocks (0 = unchecked); an id outside [0, num_blocks), or negative, reads nothing,
+ * gets checksum 0 and raises GOLLEK_STATUS_BAD_BLOCK_ID.  Asynchronous on `stream`.
  */
-GOLLEK_API int gollek_kv_block_checksum(const void *pool, const int *blocks, int n, long long block_stride,
-                             long long bytes_per_block, unsigned long long *checksums,
-                             void *stream);
+GOLLEK_API int gollek_kv_block_checksum(const void *pool, const int *blocks, int n, int num_blocks,
+                             long long block_stride, long long bytes_per_block,
+                             unsigned long long *checksums, void *stream);
 
 /* Enables `device` to access `peer_device`'s memory (idempotent). */
 GOLLEK_API int gollek_enable_peer_access(int device, int peer_device);

@@ -68,8 +68,15 @@ def test_invalid_arguments_rejected_without_a_device(lib):
     rc = lib.gollek_kv_append(dummy, dummy, _lib.F32, None, dummy, dummy, 4, 0, dummy, dummy, None,
                               None, _lib.I4, 1, 1, 63, 16, 0, 0, 0, 0, None)
     assert rc == _lib.ERR_UNSUPPORTED  # odd head_dim for int4
-    rc = lib.gollek_kv_migrate(dummy, None, dummy, dummy, dummy, dummy, 1, 16, 16, 16, 0, None)
+    rc = lib.gollek_kv_migrate(dummy, None, dummy, dummy, dummy, dummy, 1, 0, 0, 16, 16, 16, 0, None)
     assert rc == _lib.ERR_INVALID_ARGUMENT  # src_v NULL but dst_v set
+    rc = lib.gollek_kv_migrate(dummy, dummy, dummy, dummy, dummy, dummy, 1, 4, 4, 16, 16, 32, 0, None)
+    assert rc == _lib.ERR_INVALID_ARGUMENT  # a bounded pool's blocks would overlap
+    rc = lib.gollek_kv_migrate(dummy, dummy, dummy, dummy, dummy, dummy, 1, -1, 4, 16, 16, 16, 0, None)
+    assert rc == _lib.ERR_INVALID_ARGUMENT  # negative pool size
+    rc = lib.gollek_kv_append(dummy, dummy, _lib.F32, None, dummy, dummy, 4, 0, dummy, dummy, dummy,
+                              dummy, _lib.I8, 1, 1, 64, 16, 0, 8, 1, 0, None)
+    assert rc == _lib.ERR_UNSUPPORTED  # int8 append into per-(page, head) scales
 
 
 def test_prefill_arguments_rejected_without_a_device(lib):

@@ -155,6 +155,52 @@ def test_migrate_unaligned_bytes_path(cuda_device):
     assert np.array_equal(db.cpu().numpy(), ref)
 
 
+def test_migrate_skips_out_of_range_ids(cuda_device):
+    """Ids outside a pool (negative, or >= the pool's block count) are skipped on the
+    device and raise GOLLEK_STATUS_BAD_BLOCK_ID; the valid copies of the same call land.
+    The ids are checked before any address is formed, so nothing outside the pools is
+    touched (local memory only)."""
+    from gollek_b200 import _lib, ops
+    ops.device_status(cuda_device.index, clear=True)
+    bpb, nb = 4096, 12
+    rng = np.random.default_rng(21)
+    a = rng.integers(0, 256, nb * bpb, dtype=np.uint8)
+    b = rng.integers(0, 256, nb * bpb, dtype=np.uint8)
+    src = np.array([1, nb, 4, -1, 6], np.int32)
+    dst = np.array([0, 2, nb + 5, 9, 11], np.int32)
+    ref = b.copy()
+    for s_, d_ in zip(src, dst):
+        if 0 <= s_ < nb and 0 <= d_ < nb:
+            ref[d_ * bpb:(d_ + 1) * bpb] = a[s_ * bpb:(s_ + 1) * bpb]
+    da, db = _t(a, cuda_device), _t(b, cuda_device)
+    ops.kv_migrate(da, None, db, None, _t(src, cuda_device), _t(dst, cuda_device),
+                   src_block_stride=bpb, dst_block_stride=bpb, bytes_per_block=bpb)
+    torch.cuda.synchronize()
+    assert np.array_equal(db.cpu().numpy(), ref)
+    assert ops.device_status(cuda_device.index, clear=True) & _lib.STATUS_BAD_BLOCK_ID
+    # the byte-granular kernel checks the same way
+    db2 = _t(b, cuda_device)
+    ops.kv_migrate(da[:nb * bpb - 3], None, db2, None, _t(src, cuda_device), _t(dst, cuda_device),
+                   src_block_stride=bpb, dst_block_stride=bpb, bytes_per_block=bpb - 3)
+    torch.cuda.synchronize()
+    ref2 = b.copy()
+    for s_, d_ in zip(src, dst):
+        if 0 <= s_ < nb and 0 <= d_ < nb:
+            ref2[d_ * bpb:d_ * bpb + bpb - 3] = a[s_ * bpb:s_ * bpb + bpb - 3]
+    assert np.array_equal(db2.cpu().numpy(), ref2)
+    assert ops.device_status(cuda_device.index, clear=True) & _lib.STATUS_BAD_BLOCK_ID
+    # checksums: a bad id reads nothing and reports 0
+    got = ops.block_checksums(da, _t(np.array([3, nb, -2], np.int32), cuda_device),
+                              block_stride=bpb, bytes_per_block=bpb).cpu().numpy()
+    assert got[1] == 0 and got[2] == 0 and got[0] != 0
+    assert ops.device_status(cuda_device.index, clear=True) & _lib.STATUS_BAD_BLOCK_ID
+    # a clean call leaves the status clear
+    ops.kv_migrate(da, None, db, None, _t(np.array([2], np.int32), cuda_device),
+                   _t(np.array([3], np.int32), cuda_device), src_block_stride=bpb,
+                   dst_block_stride=bpb, bytes_per_block=bpb)
+    assert ops.device_status(cuda_device.index, clear=True) == 0
+
+
 def test_block_checksums_match_numpy(cuda_device):
     from gollek_b200 import ops
     rng = np.random.default_rng(14)
