@@ -1,24 +1,30 @@
 """Benchmark of the paged-KV hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode_bf16|decode_int8|decode_fp32|longctx|migrate|config1|
-                                prefill|prefill_int8|cow] [--tq T]
+                    [--workload default|decode_bf16|decode_int8|decode_fp32|longctx|migrate|
+                                config1|prefill|prefill_int8|cow] [--tq T]
 
-Default workload: Llama-3-8B-shaped bf16 decode attention, 32 query
-heads over 8 KV heads, head_dim 128, block 16, 64 sequences with context lengths
+Default line (BASELINE config 2 as the headline): Llama-3-8B-shaped bf16 decode attention,
+32 query heads over 8 KV heads, head_dim 128, block 16, 64 sequences with context lengths
 U[512, 8192] per GPU, pages a random permutation of the pool.  One step = one decode
-attention launch over the batch.  At N GPUs each rank decodes its own 64-sequence
-batch (sequences are independent units; no collective on the data path): weak scaling.
+attention launch over the batch.  At N GPUs each rank decodes its own 64-sequence batch
+with the same lengths and page tables as every other rank (its own q/K/V values):
+sequences are independent units, no collective on the data path, weak scaling.  The same
+line carries the other BASELINE configs, measured in the same run:
+  config1      config 1 through the legacy synchronous symbol paged_attention_launch
+  decode_int8  config 3: int8 KV with per-(page, head) scales
+  longctx      config 5: KV heads sharded over the N GPUs (8/N each), strong scaling
+  migrate      config 4 (N >= 2): prefill ranks [0, N/2) push KV blocks to decode ranks
+               [N/2, N) over NVLink, checked bit for bit by block checksums
 
-Other workloads (run by hand, one JSON line each): decode_int8 (config 3), decode_fp32,
-longctx (config 5, KV heads sharded over the ranks, strong scaling), migrate (config 4,
-prefill ranks push KV blocks to decode ranks over NVLink), config1 (the legacy fp32
-symbol on config 1), prefill / prefill_int8 (multi-query causal attention, T query
-tokens per sequence over config 2's bf16 or config 3's int8 pool), cow (prompt-cache
-copy-on-write block copy inside one GPU's pool, config 4's block layout).
+--workload X runs one of these alone (one JSON line), or decode_fp32, prefill /
+prefill_int8 (multi-query causal attention, T query tokens per sequence over config 2's
+bf16 or config 3's int8 pool), cow (prompt-cache copy-on-write block copy inside one
+GPU's pool, config 4's block layout).
 
---impl reference times the reference's own CPU algorithm for the same workload: the
-C restatement in oracle/ (the reference is Java; no JDK exists here), all host threads.
+--impl reference times the reference's own CPU algorithm for the same workload and the
+same aggregate work (N batches at N GPUs): the C restatement in oracle/ (the reference is
+Java; no JDK exists here), on all host threads.
 """
 from __future__ import annotations
 
@@ -45,9 +51,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode_bf16",
-                    choices=["decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate", "config1",
-                             "prefill", "prefill_int8", "cow"])
+    ap.add_argument("--workload", default="default",
+                    choices=["default", "decode_bf16", "decode_int8", "decode_fp32", "longctx", "migrate",
+                             "config1", "prefill", "prefill_int8", "cow"])
     ap.add_argument("--tq", type=int, default=4, help="prefill: query tokens per sequence")
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--gather", action="store_true", help="longctx: all-gather head-sharded outputs")
@@ -97,7 +103,9 @@ def context_lengths(shape, rng):
 class DecodeBatch:
     """Synthetic decode batch resident in HBM: pool, tables, q, output."""
 
-    def __init__(self, workload, seed, device, head_lo=0, head_hi=None):
+    def __init__(self, workload, seed, device, head_lo=0, head_hi=None, value_seed=None):
+        """seed draws the context lengths and the page tables (the same on every rank, so
+        every rank has the same work); value_seed (default: seed) draws q, K and V."""
         import numpy as np
         import torch
         sh = decode_shape(workload)
@@ -121,7 +129,7 @@ class DecodeBatch:
             off += need[s]
         self.bt_np = bt
         self.device = device
-        g = torch.Generator(device=device).manual_seed(seed)
+        g = torch.Generator(device=device).manual_seed(seed if value_seed is None else value_seed)
         kv_dt = {"decode_fp32": torch.float32}.get(workload, torch.bfloat16)
         q_dt = torch.float32 if workload == "decode_fp32" else torch.bfloat16
         std = 1.0 if workload == "decode_fp32" else 0.5
@@ -171,13 +179,8 @@ class DecodeBatch:
     def algorithmic_bytes(self):
         """Bytes one decode step must move: every context token's K and V row of each
         kv-head, the scales, q, out, the used block-table entries and the lengths."""
-        sh = self.sh
-        tok = int(self.ctx_np.sum())
-        kv = tok * self.hkv * sh["d"] * self.kv_elem * 2
-        pages = int(((self.ctx_np + sh["bs"] - 1) // sh["bs"]).sum())
-        scales = pages * self.hkv * 4 * 2 if self.k_scales is not None else 0
-        qo = 2 * self.q.numel() * self.q_elem
-        return kv + scales + qo + pages * 4 + len(self.ctx_np) * 4
+        return decode_alg_bytes(self.sh, self.ctx_np, self.hkv, self.kv_elem, self.q_elem,
+                                self.q.numel(), self.k_scales is not None)
 
     def run(self, out=None, q=None, bt=None, ctx=None, stream=None, workspace=None):
         from gollek_b200 import ops
@@ -293,82 +296,130 @@ def sum_over_ranks(x, world):
 
 # ------------------------------------------------------------------ CPU baseline
 
-def cpu_decode_baseline(batch, seconds, threads=None, q=None, tq=1):
+def cpu_decode_baseline(batch, seconds, threads=None, q=None, tq=1, max_seqs=None):
     """The reference's CPU algorithm (oracle restatement of PagedAttentionVectorAPI) on
-    fp32 copies of the same values, all host threads, whole batch per step.  q/tq: a
-    multi-query step ([S, tq, Hq, D] queries at each sequence's last tq positions)."""
+    fp32 copies of the same values, all host threads.  q/tq: a multi-query step
+    ([S, tq, Hq, D] queries at each sequence's last tq positions).
+
+    Bounded sample: the first n sequences of the batch, n doubled until one call takes
+    about a third of `seconds`; only their pages are gathered to the host.  The step time
+    is scaled to the whole batch by context tokens (the work is linear in them)."""
     import numpy as np
+    import torch
     from oracle import oracle as O
-    threads = threads or O.num_threads()
-    q = (batch.q if q is None else q).float().cpu().numpy()
-    if q.ndim == 3:
-        q = q[:, None]
-    bt, ctx = batch.bt_np, batch.ctx_np
-    # int8 pages: the oracle's INT8 storage with per-token scales (the page scale repeated)
-    if batch.k_scales is not None:
-        k = batch.k.cpu().numpy()
-        v = batch.v.cpu().numpy()
-        bs = batch.sh["bs"]
-        ks = np.repeat(batch.k_scales.cpu().numpy()[:, :, None], bs, axis=2)
-        vs = np.repeat(batch.v_scales.cpu().numpy()[:, :, None], bs, axis=2)
-        storage = O.INT8
-    else:
-        k = batch.k.float().cpu().numpy()
-        v = batch.v.float().cpu().numpy()
-        ks = vs = None
-        storage = O.FP32
+    threads = threads or host_cores()
+    qa = (batch.q if q is None else q)
+    bt_all, ctx_all = batch.bt_np, batch.ctx_np
+    bs = batch.sh["bs"]
+    B = len(ctx_all)
+    n_cap = B if max_seqs is None else max_seqs
     scale = 1.0 / math.sqrt(batch.sh["d"])
-    # bounded sample: grow the number of sequences until one call takes ~1/3 of the budget
-    B = len(ctx)
+
+    def sample(n):
+        need = (ctx_all[:n] + bs - 1) // bs
+        pages = np.concatenate([bt_all[i, :need[i]] for i in range(n)]).astype(np.int64)
+        remap = np.zeros_like(bt_all[:n])
+        off = 0
+        for i in range(n):
+            remap[i, :need[i]] = np.arange(off, off + need[i], dtype=np.int32)
+            off += need[i]
+        idx = torch.from_numpy(pages).to(batch.k.device)
+        qs = qa[:n].float().cpu().numpy()
+        if qs.ndim == 3:
+            qs = qs[:, None]
+        if batch.k_scales is not None:
+            k = batch.k.index_select(0, idx).cpu().numpy()
+            v = batch.v.index_select(0, idx).cpu().numpy()
+            ks = np.repeat(batch.k_scales.index_select(0, idx).cpu().numpy()[:, :, None], bs, axis=2)
+            vs = np.repeat(batch.v_scales.index_select(0, idx).cpu().numpy()[:, :, None], bs, axis=2)
+            st = O.INT8
+        else:
+            k = batch.k.index_select(0, idx).float().cpu().numpy()
+            v = batch.v.index_select(0, idx).float().cpu().numpy()
+            ks = vs = None
+            st = O.FP32
+        return qs, k, v, remap, ctx_all[:n].copy(), ks, vs, st
+
+    def call(smp):
+        qs, k, v, bt, ctx, ks, vs, st = smp
+        O.a2_compute(qs, k, v, bt, ctx, scale, storage=st, num_kv_heads=batch.hkv, block_size=bs,
+                     k_scale=ks, v_scale=vs, threads=threads)
+
     n = 1
     while True:
+        smp = sample(n)
         t0 = time.perf_counter()
-        O.a2_compute(q[:n], k, v, bt[:n], ctx[:n], scale, storage=storage,
-                     num_kv_heads=batch.hkv, block_size=batch.sh["bs"], k_scale=ks, v_scale=vs,
-                     threads=threads)
+        call(smp)
         dt = time.perf_counter() - t0
-        if n >= B or dt > seconds / 3:
+        if n >= n_cap or dt > seconds / 3:
             break
-        n = min(B, n * 2)
+        n = min(n_cap, n * 2)
     reps, total, t_start = 0, 0.0, time.perf_counter()
     while time.perf_counter() - t_start < seconds and reps < 1000:
         t0 = time.perf_counter()
-        O.a2_compute(q[:n], k, v, bt[:n], ctx[:n], scale, storage=storage,
-                     num_kv_heads=batch.hkv, block_size=batch.sh["bs"], k_scale=ks, v_scale=vs,
-                     threads=threads)
+        call(smp)
         total += time.perf_counter() - t0
         reps += 1
-    per_seq = total / (reps * n)
-    # tokens/s over the whole batch: the sample's time per sequence, weighted by context
-    frac = float(ctx[:n].sum()) / float(ctx.sum())
+    frac = float(ctx_all[:n].sum()) / float(ctx_all.sum())
     t_step = (total / reps) / frac
     return {"value": B * tq / t_step, "unit": "tokens/s" if tq == 1 else "query tokens/s",
             "cores": int(threads), "kind": "port",
-            "sample": f"{n} of {B} sequences ({frac:.1%} of the batch's context tokens), "
-                      f"{reps} repetitions, {total:.1f} s; scaled to the full batch by context "
-                      f"tokens; oracle/oracle.c a2 (PagedAttentionVectorAPI restatement), "
-                      f"fp32 values, OpenMP over (sequence, q-head)",
-            "seconds_per_step": t_step, "per_seq_s": per_seq}
+            "sample": f"{n} of {B} sequences ({frac:.1%} of the batch's context tokens, "
+                      f"{batch.hkv} kv heads), {reps} repetitions, {total:.1f} s; scaled to the "
+                      f"full batch by context tokens; oracle/oracle.c a2 (PagedAttentionVectorAPI "
+                      f"restatement), fp32 values, OpenMP over (sequence, q-head)",
+            "seconds_per_step": t_step, "per_seq_s": (total / reps) / n}
 
 
 # ------------------------------------------------------------------ decode bench
 
-def bench_decode(args, world, rank, local):
+def host_cores() -> int:
+    """Host threads this process may use (the CPU arms use all of them, whatever
+    OMP_NUM_THREADS a launcher set)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def decode_config(workload, world, ctx_np, alg_bytes, hkv_per_gpu):
+    """The `config` dict of a decode line -- the same for our arm and the reference arm."""
+    sh = decode_shape(workload)
+    tok = int(ctx_np.sum())
+    shard = workload == "longctx"
+    return {
+        "workload": WORKLOAD_NAMES[workload],
+        "batch_per_gpu": sh["batch"],
+        "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"], "head_dim": sh["d"],
+        "block_size": sh["bs"], "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
+        "context_tokens_per_gpu": tok,
+        "context_tokens_total": tok if shard else tok * world,
+        "kv_heads_per_gpu": hkv_per_gpu,
+        "parallelism": (f"kv-head shard x{world}" if shard
+                        else f"independent batches x{world} (same lengths and tables on every rank)"),
+        "l2": f"no flush: {alg_bytes / 1e9:.2f} GB of KV per step per GPU > 126 MB L2",
+    }
+
+
+def bench_decode(args, world, rank, local, workload=None, steps=None, cpu=True):
+    """One decode workload; returns its JSON line (a dict) on rank 0, None elsewhere."""
     import numpy as np
     import torch
     from gollek_b200 import ops
+    workload = workload or args.workload
+    steps = steps or args.steps
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if args.workload == "longctx":
+    if workload == "longctx":
         from gollek_b200.sharding import kv_head_shard
         lo, hi = kv_head_shard(decode_shape("longctx")["hkv"], world, rank)
         batch = DecodeBatch("longctx", args.seed, dev, head_lo=lo, head_hi=hi)
     else:
-        batch = DecodeBatch(args.workload, args.seed + rank, dev)
+        # every rank: the same lengths and page tables (equal work), its own values
+        batch = DecodeBatch(workload, args.seed, dev, value_seed=args.seed + rank)
     stream = torch.cuda.current_stream(dev)
     gather_buf = None
-    if args.workload == "longctx" and args.gather and world > 1:
-        import torch.distributed as dist
+    if workload == "longctx" and args.gather and world > 1:
         gather_buf = torch.empty((world,) + tuple(batch.out.shape), dtype=batch.out.dtype, device=dev)
 
     def step():
@@ -385,7 +436,7 @@ def bench_decode(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
@@ -393,18 +444,18 @@ def bench_decode(args, world, rank, local):
     t_ms = e0.elapsed_time(e1)
     t_ms_max = max_over_ranks(t_ms, world)
     B = len(batch.ctx_np)
-    launches = args.steps * (1 + (1 if gather_buf is not None else 0))
+    launches = steps * (1 + (1 if gather_buf is not None else 0))
 
     # ---------------- e2e: host buffers in, host result out, through the C ABI
     from gollek_b200 import _lib
     B, Hq, D = batch.q.shape
-    append = args.workload in ("decode_bf16", "decode_fp32", "longctx")
+    append = workload in ("decode_bf16", "decode_fp32", "longctx")
     # The step's host inputs sit in one pinned staging block (q, tables, lengths and, with
     # the append, the new K/V rows and their positions), so a step moves them with one
     # H2D copy; the output comes back with one D2H copy.
     parts = [("q", batch.q.cpu()), ("bt", batch.bt.cpu()), ("ctx", batch.ctx.cpu())]
     if append:
-        g = torch.Generator().manual_seed(args.seed + 7)
+        g = torch.Generator().manual_seed(args.seed + 7 + rank)
         kv_dt = batch.k.dtype
         parts += [("k_new", torch.randn((B, batch.hkv, D), generator=g).to(kv_dt)),
                   ("v_new", torch.randn((B, batch.hkv, D), generator=g).to(kv_dt)),
@@ -466,7 +517,7 @@ def bench_decode(args, world, rank, local):
 
     graph_note = ("double-buffered pipeline on 3 streams: H2D of step k+1 and D2H of step k-1 "
                   "overlap the decode of step k")
-    e2e_steps = max(1, min(args.steps, 100))
+    e2e_steps = max(1, min(steps, 100))
     for k in range(max(2, args.warmup)):
         pipe_step(k)
     torch.cuda.synchronize()
@@ -485,78 +536,83 @@ def bench_decode(args, world, rank, local):
     h2d = h_stage.numel()
     d2h = hout_pin.numel() * hout_pin.element_size()
 
-    if args.workload == "longctx":
+    if workload == "longctx":
         total_seqs = B  # every rank processes all sequences for its heads
     else:
         total_seqs = B * world
-    value = total_seqs * args.steps / (t_ms_max / 1e3)
+    value = total_seqs * steps / (t_ms_max / 1e3)
     e2e_value = total_seqs * e2e_steps / (e2e_ms / 1e3)
 
-    # roofline of the decode kernel (this rank's launch; max over ranks)
+    # roofline of the decode kernel (this rank's launch; the slowest rank's rate)
     alg = batch.algorithmic_bytes()
-    per_launch_s = (t_ms / 1e3) / args.steps
+    per_launch_s = (t_ms / 1e3) / steps
     achieved = alg / per_launch_s / 1e9
     achieved_min = -max_over_ranks(-achieved, world)
+    alg_total = sum_over_ranks(float(alg), world)
     peak, peak_kind = peaks()
-    traffic = traffic_per_launch(args.workload)
+    traffic = traffic_per_launch(workload)
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload != "longctx":
-        cpu = cpu_decode_baseline(batch, args.cpu_seconds)
-        cpu.pop("per_seq_s", None)
-        cpu.pop("seconds_per_step", None)
+    cpu_line = None
+    if cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_line = cpu_decode_baseline(batch, args.cpu_seconds)
+        cpu_line.pop("per_seq_s", None)
+        cpu_line.pop("seconds_per_step", None)
 
     clocks = clk.summary()
-    if rank == 0:
-        sh = batch.sh
-        line = {
-            "metric": METRIC,
-            "value": value,
-            "unit": "tokens/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": t_ms_max / args.steps,
-            "higher_is_better": True,
-            "scaling": "strong" if args.workload == "longctx" else "weak",
-            "vs_baseline": None,
-            "dtype": {"decode_fp32": "f32", "decode_int8": "int8 KV, bf16 q/out, f32 accumulate"}
-            .get(args.workload, "bf16 KV/q/out, f32 accumulate"),
-            "data": "synthetic (seeded; BASELINE shapes and distributions)",
-            "config": {
-                "workload": WORKLOAD_NAMES[args.workload],
-                "batch_per_gpu": B if args.workload != "longctx" else B,
-                "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"], "head_dim": sh["d"],
-                "block_size": sh["bs"], "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
-                "context_tokens_per_gpu": int(batch.ctx_np.sum()),
-                "kv_heads_per_gpu": batch.hkv,
-                "parallelism": (f"kv-head shard x{world}" if args.workload == "longctx"
-                                else f"independent batches x{world}"),
-                "l2": f"no flush: {alg / 1e9:.2f} GB of KV per step per GPU > 126 MB L2",
-            },
-            "hbm_gbs": achieved_min,
-            "context_tokens_per_s": float(batch.ctx_np.sum()) * (world if args.workload != "longctx" else 1)
-            * args.steps / (t_ms_max / 1e3),
-            "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
-                         "frac": achieved_min / peak, "traffic": traffic,
-                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                         "algorithmic_bytes_per_launch": alg,
-                         "kernel": "decode_tma_kernel"},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "wall_s": wall,
-                    "path": "pinned host staging block (q, tables, lengths, new K/V rows) -> one H2D -> "
-                            "gollek_kv_append -> gollek_paged_attention_v2 -> one D2H of out"
-                            if append else
-                            "pinned host staging block (q, tables, lengths) -> one H2D -> "
-                            "gollek_paged_attention_v2 -> one D2H of out",
-                    "gpu_launches_per_step": 2 if append else 1,
-                    "execution": graph_note},
-            "gpu_launches": launches,
-            "clocks": clocks,
-            "cpu_baseline": cpu,
-        }
-        print(json.dumps(line), flush=True)
+    ctx_np = batch.ctx_np
+    hkv = batch.hkv
+    del batch, d_stages, dv, outs, ws_e2e, d_stage, gather_buf
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": args.warmup,
+        "ms_per_step": t_ms_max / steps,
+        "higher_is_better": True,
+        "scaling": "strong" if workload == "longctx" else "weak",
+        "vs_baseline": None,
+        "dtype": {"decode_fp32": "f32", "decode_int8": "int8 KV, bf16 q/out, f32 accumulate"}
+        .get(workload, "bf16 KV/q/out, f32 accumulate"),
+        "data": "synthetic (seeded; BASELINE shapes and distributions)",
+        "config": decode_config(workload, world, ctx_np, alg, hkv),
+        "hbm_gbs": achieved_min,
+        "hbm_gbs_aggregate": alg_total * steps / (t_ms_max / 1e3) / 1e9,
+        "context_tokens_per_s": float(ctx_np.sum()) * (world if workload != "longctx" else 1)
+        * steps / (t_ms_max / 1e3),
+        "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_min / peak, "traffic": traffic,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                     "algorithmic_bytes_per_launch": alg,
+                     "achieved_is": "the slowest rank's algorithmic bytes per launch / its launch time",
+                     "kernel": "decode_tma_kernel"},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "wall_s": wall,
+                "path": "pinned host staging block (q, tables, lengths, new K/V rows) -> one H2D -> "
+                        "gollek_kv_append -> gollek_paged_attention_v2 -> one D2H of out"
+                        if append else
+                        "pinned host staging block (q, tables, lengths) -> one H2D -> "
+                        "gollek_paged_attention_v2 -> one D2H of out",
+                "gpu_launches_per_step": 2 if append else 1,
+                "execution": graph_note},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "cpu_baseline": cpu_line,
+    }
+    if workload == "longctx":
+        line["limiter"] = ("no exchange inside attention (KV-head shards are independent); each "
+                           "GPU streams its heads' pages, so strong scaling follows per-GPU HBM "
+                           "time, and the head split is exact (every head has the same tokens)")
+    elif world > 1:
+        line["limiter"] = ("none across GPUs: independent batches with equal work; NCCL carries "
+                           "only the barrier and the timing all-reduce")
+    return line
 
 
 # ------------------------------------------------------------------ migration bench
@@ -574,13 +630,19 @@ def migrate_plan(seed, world):
     return lens, src_rank, blocks, nsrc
 
 
-def bench_migrate(args, world, rank, local):
+NVLINK_NOMINAL_GBS = 900.0   # NVLink 5, per direction per GPU (NVIDIA's B200 figure)
+NVLINK_PEER_COPY_GBS = 770.0  # peer copy per direction measured on this pool of B200s
+
+
+def bench_migrate(args, world, rank, local, steps=None):
+    """Config 4 migration; returns its JSON line (a dict) on rank 0, None elsewhere."""
     import numpy as np
     import torch
     import torch.distributed as dist
     from gollek_b200 import _lib, ops
     if world < 2:
         raise SystemExit("migrate needs --gpus >= 2 (prefill ranks push to decode ranks)")
+    steps = steps or args.steps
     dev = torch.device("cuda", local)
     L, H, BS, D = 32, 8, 16, 128
     bpb = BS * H * D * 2  # bytes per (block, layer), bf16: 32 KiB
@@ -635,7 +697,8 @@ def bench_migrate(args, world, rank, local):
     def step():
         if is_src:
             ops.kv_migrate(k, v, None, None, s_ids, d_ids, src_block_stride=blk, dst_block_stride=blk,
-                           bytes_per_block=blk, device=local, dst_k_ptr=dk_ptr, dst_v_ptr=dv_ptr)
+                           bytes_per_block=blk, device=local, dst_k_ptr=dk_ptr, dst_v_ptr=dv_ptr,
+                           src_num_blocks=pool_blocks, dst_num_blocks=pool_blocks)
 
     for _ in range(args.warmup):
         step()
@@ -645,13 +708,19 @@ def bench_migrate(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
     t_ms = e0.elapsed_time(e1) if is_src else 0.0
     t_max = max_over_ranks(t_ms, world)
+    # every source rank's own link rate; the slowest one bounds the step
+    my_bytes = float(nblk * blk * 2) if is_src else 0.0
+    link_gbs = my_bytes * steps / (t_ms / 1e3) / 1e9 if is_src and t_ms > 0 else float("inf")
+    link_min = -max_over_ranks(-link_gbs, world)
+    status_bits = ops.device_status(local, clear=True)
+    bad = max_over_ranks(float(status_bits), world)
     # verification: per-block checksums on both sides must agree (bit-exact copy)
     ids = s_ids if is_src else d_ids
     ck = ops.block_checksums(k, ids, block_stride=blk, bytes_per_block=blk).cpu().numpy()
@@ -664,27 +733,41 @@ def bench_migrate(args, world, rank, local):
     if is_src:
         lib.gollek_ipc_close_handle(ctypes.c_void_p(base_k))
         lib.gollek_ipc_close_handle(ctypes.c_void_p(base_v))
+    clocks = clk.summary()
+    del k, v, s_ids, d_ids
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
     barrier(world)
-    if rank == 0:
-        gbs = bytes_total * args.steps / (t_max / 1e3) / 1e9
-        peak = 770.0 * nsrc
-        print(json.dumps({
-            "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "u8 (bf16 KV bytes)",
-            "data": "synthetic (seeded; BASELINE config 4 shapes)",
-            "config": {"workload": "config4_prefill_to_decode_migration", "layers": L,
-                       "kv_heads": H, "head_dim": D, "block_size": BS, "requests": 64,
-                       "prompt": "loguniform[2048,32768]", "blocks": int(blocks.sum()),
-                       "bytes_per_step": bytes_total, "sources": nsrc, "destinations": nsrc,
-                       "parallelism": f"{nsrc} prefill ranks -> {nsrc} decode ranks, NVLink P2P push"},
-            "bit_exact": bool(ok),
-            "roofline": {"bound": "nvlink", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                         "frac": gbs / peak, "traffic": None,
-                         "peak_source": "770 GB/s measured peer copy per direction per source GPU"},
-            "gpu_launches": args.steps * nsrc, "clocks": clk.summary(),
-            "cpu_baseline": None if args.no_cpu_baseline else cpu_migrate_baseline(args.seed),
-        }), flush=True)
+    if rank != 0:
+        return None
+    gbs = bytes_total * steps / (t_max / 1e3) / 1e9
+    peak = NVLINK_NOMINAL_GBS * nsrc
+    return {
+        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": t_max / steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "u8 (bf16 KV bytes)",
+        "data": "synthetic (seeded; BASELINE config 4 shapes)",
+        "config": {"workload": "config4_prefill_to_decode_migration", "layers": L,
+                   "kv_heads": H, "head_dim": D, "block_size": BS, "requests": 64,
+                   "prompt": "loguniform[2048,32768]", "blocks": int(blocks.sum()),
+                   "bytes_per_step": bytes_total, "sources": nsrc, "destinations": nsrc,
+                   "parallelism": f"{nsrc} prefill ranks -> {nsrc} decode ranks, NVLink P2P push "
+                                  "(plain 16-byte peer stores through a CUDA-IPC mapping)",
+                   "l2": f"no flush: {bytes_total / nsrc / 1e9:.1f} GB moved per source per step"},
+        "bit_exact": bool(ok) and bad == 0,
+        "roofline": {"bound": "nvlink", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                     "frac": gbs / peak, "traffic": None,
+                     "peak_source": f"NVLink 5 nominal {NVLINK_NOMINAL_GBS:.0f} GB/s per direction "
+                                    f"x {nsrc} source GPU(s)",
+                     "frac_of_measured_peer_copy": gbs / (NVLINK_PEER_COPY_GBS * nsrc),
+                     "measured_peer_copy_source": f"{NVLINK_PEER_COPY_GBS:.0f} GB/s per direction: "
+                                                  "the peer copy measured on this pool of B200s",
+                     "slowest_source_gbs": link_min,
+                     "kernel": "kv_migrate_kernel_v16"},
+        "limiter": "each source GPU's NVLink egress (one destination per source, plain peer stores)",
+        "gpu_launches": steps * nsrc, "clocks": clocks,
+        "cpu_baseline": None,
+    }
 
 
 def config1_case(seed):
@@ -724,12 +807,13 @@ def cpu_config1_baseline(seed, seconds=10.0):
                       "oracle_a1_execute (PagedAttentionCpuFallback restatement), one thread"}
 
 
-def bench_config1(args, world, rank, local):
+def bench_config1(args, world, rank, local, steps=None):
     """BASELINE config 1 through the legacy synchronous symbol paged_attention_launch (the
     reference's FFM entry point): latency-bound at 4 sequences, reported as tokens/s with
     the GB/s of its 4 MB step."""
     import torch
     from gollek_b200 import ops
+    steps = steps or args.steps
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     q, k, v, bt, ctx, scale, alg = config1_case(args.seed)
@@ -748,7 +832,7 @@ def bench_config1(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record(per_thread)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         e1.record(per_thread)
         torch.cuda.synchronize()
@@ -756,7 +840,7 @@ def bench_config1(args, world, rank, local):
     # e2e: pinned host q, tables, lengths -> H2D -> the legacy call -> D2H of out
     hq, hbt, hctx = (torch.from_numpy(x).pin_memory() for x in (q, bt, ctx))
     hout = torch.empty_like(out, device="cpu").pin_memory()
-    e2e_steps = max(1, min(args.steps, 200))
+    e2e_steps = max(1, min(steps, 200))
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(per_thread)
     for _ in range(e2e_steps):
@@ -770,17 +854,20 @@ def bench_config1(args, world, rank, local):
     f1.record(per_thread)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    del dq, dk, dv, dbt, dctx, out
+    torch.cuda.empty_cache()
     if rank != 0:
-        return
-    per_s = t_ms / 1e3 / args.steps
+        return None
+    per_s = t_ms / 1e3 / steps
     gbs = alg / per_s / 1e9
     peak, peak_kind = peaks()
-    cpu = None if args.no_cpu_baseline or world > 1 else cpu_config1_baseline(args.seed)
+    cpu = None if args.no_cpu_baseline or world > 1 else cpu_config1_baseline(
+        args.seed, seconds=min(10.0, args.cpu_seconds))
     if cpu:
         cpu.pop("seconds_per_step", None)
-    print(json.dumps({
+    return {
         "metric": METRIC, "value": 4 * world / per_s, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms / args.steps,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": t_ms / steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded; BASELINE config 1)",
         "config": {"workload": "config1_fp32_mha_decode_legacy_symbol", "batch_per_gpu": 4,
@@ -796,8 +883,8 @@ def bench_config1(args, world, rank, local):
                 "h2d_bytes_per_step": q.nbytes + bt.nbytes + ctx.nbytes, "d2h_bytes_per_step": q.nbytes,
                 "steps": e2e_steps,
                 "path": "pinned host q/tables/lengths -> H2D -> paged_attention_launch -> D2H out"},
-        "gpu_launches": args.steps, "clocks": clk.summary(), "cpu_baseline": cpu,
-    }), flush=True)
+        "gpu_launches": steps, "clocks": clk.summary(), "cpu_baseline": cpu,
+    }
 
 
 def cpu_migrate_baseline(seed, seconds=3.0, sample_blocks=128):
@@ -1072,7 +1159,11 @@ def bench_reference(args):
         pass
 
     import torch
-    sh = decode_shape(args.workload)
+    threads = host_cores()
+    torch.set_num_threads(threads)
+    workload = "decode_bf16" if args.workload == "default" else args.workload
+    sh = decode_shape(workload)
+    # the GPU arm's lengths and page tables (the same seed), values drawn on the host
     rng = np.random.default_rng(args.seed)
     ctx = context_lengths(sh, rng)
     B, BS, D = sh["batch"], sh["bs"], sh["d"]
@@ -1081,56 +1172,107 @@ def bench_reference(args):
     perm = rng.permutation(nb).astype(np.int32)
     bt = np.zeros((B, int(need.max())), np.int32)
     off = 0
-    for s in range(B):
-        bt[s, :need[s]] = perm[off:off + need[s]]
-        off += need[s]
+    for s_ in range(B):
+        bt[s_, :need[s_]] = perm[off:off + need[s_]]
+        off += need[s_]
     hkv = sh["hkv"]
-    if args.workload == "longctx":
+    if workload == "longctx":
         hkv = max(1, hkv // max(world, 1))
     hq = sh["hq"] // sh["hkv"] * hkv
     g = torch.Generator().manual_seed(args.seed)
-    std = 1.0 if args.workload == "decode_fp32" else 0.5
+    std = 1.0 if workload == "decode_fp32" else 0.5
+    to = torch.float32 if workload == "decode_fp32" else torch.bfloat16
+    elem = 4 if to == torch.float32 else 2
+    # The sample is drawn from the first sequences, so the host pool holds only their
+    # pages (at most ~1.5 GB of K and V: config 5's whole pool would not fit in reason).
+    page_bytes = hkv * BS * D * elem * 2
+    cum = np.cumsum(need) * page_bytes
+    max_seqs = max(1, int(np.searchsorted(cum, 1.5e9, side="right")))
+    max_seqs = min(B, max_seqs)
+    nb_host = int(need[:max_seqs].sum())
+    perm_h = rng.permutation(nb_host).astype(np.int32)
+    bt = np.zeros_like(bt)
+    off = 0
+    for s_ in range(max_seqs):
+        bt[s_, :need[s_]] = perm_h[off:off + need[s_]]
+        off += need[s_]
     hb = HostBatch()
     hb.sh, hb.hkv, hb.ctx_np, hb.bt_np = sh, hkv, ctx, bt
     # values rounded to bf16 as on the GPU arm (fp32 stays fp32)
-    to = torch.float32 if args.workload == "decode_fp32" else torch.bfloat16
     hb.q = torch.randn((B, hq, D), generator=g).to(to)
-    hb.k = (torch.randn((nb, hkv, BS, D), generator=g) * std).to(to)
-    hb.v = (torch.randn((nb, hkv, BS, D), generator=g) * std).to(to)
+    hb.k = (torch.randn((nb_host, hkv, BS, D), generator=g) * std).to(to)
+    hb.v = (torch.randn((nb_host, hkv, BS, D), generator=g) * std).to(to)
     hb.k_scales = hb.v_scales = None
-    if args.workload == "decode_int8":
-        def qp(x):
-            xs = x.float()
-            amax = xs.abs().amax(dim=(2, 3))
-            s = torch.where(amax == 0, torch.ones_like(amax), amax / 127.0)
-            return torch.clamp(torch.floor(xs / s[:, :, None, None] + 0.5), -127, 127).to(torch.int8), s
-        hb.k, hb.k_scales = qp(hb.k)
-        hb.v, hb.v_scales = qp(hb.v)
+    if workload == "decode_int8":
+        hb.k, hb.k_scales = DecodeBatch._quant_pages(hb.k)
+        hb.v, hb.v_scales = DecodeBatch._quant_pages(hb.v)
+    kv_elem = hb.k.element_size()
+    alg = decode_alg_bytes(sh, ctx, hkv, kv_elem, hb.q.element_size(), hb.q.numel(),
+                           hb.k_scales is not None)
     per_step_budget = max(1.0, args.cpu_seconds / max(1, args.steps + args.warmup))
-    r = cpu_decode_baseline(hb, per_step_budget * (args.steps + args.warmup))
+    r = cpu_decode_baseline(hb, per_step_budget * (args.steps + args.warmup), threads=threads,
+                            max_seqs=max_seqs)
+    # The GPU arm decodes one batch per GPU per step (KV-head shards of one batch for
+    # config 5).  The reference arm does the same aggregate work on the host: N batches
+    # of the same lengths (so N times one batch's time), or config 5's whole batch.
+    n_batches = 1 if workload == "longctx" else world
+    t_step = r["seconds_per_step"] * n_batches
+    if workload == "longctx":
+        t_step = r["seconds_per_step"] * (sh["hkv"] // hkv)  # every head shard, one after another
+    value = B * n_batches / t_step
+    sample = (r["sample"] + f"; one step = {n_batches} batch(es) of these lengths"
+              if workload != "longctx" else r["sample"] + "; one step = all kv-head shards")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tokens/s",
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": r["seconds_per_step"] * 1e3, "higher_is_better": True,
-        "scaling": "strong" if args.workload == "longctx" else "weak", "vs_baseline": None,
+        "ms_per_step": t_step * 1e3, "higher_is_better": True,
+        "scaling": "strong" if workload == "longctx" else "weak", "vs_baseline": None,
         "dtype": "f32 (reference CPU path)", "data": "synthetic (seeded; same shapes as ours)",
-        "config": {"workload": WORKLOAD_NAMES[args.workload], "batch_per_gpu": B, "num_q_heads": sh["hq"],
-                   "num_kv_heads": sh["hkv"], "head_dim": D, "block_size": BS,
-                   "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
-                   "context_tokens_per_gpu": int(ctx.sum()), "kv_heads_per_gpu": hkv,
-                   "parallelism": (f"kv-head shard x{world}" if args.workload == "longctx"
-                                   else f"independent batches x{world}")},
-        "cpu_baseline": {"value": r["value"], "unit": "tokens/s", "cores": r["cores"],
-                         "kind": r["kind"], "sample": r["sample"]},
-        "e2e": {"value": r["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+        "config": decode_config(workload, world, ctx, alg, hkv),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": r["cores"],
+                         "kind": r["kind"], "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def decode_alg_bytes(sh, ctx_np, hkv, kv_elem, q_elem, q_numel, scales):
+    """Bytes one decode step must move (see DecodeBatch.algorithmic_bytes)."""
+    tok = int(ctx_np.sum())
+    kv = tok * hkv * sh["d"] * kv_elem * 2
+    pages = int(((ctx_np + sh["bs"] - 1) // sh["bs"]).sum())
+    sc = pages * hkv * 4 * 2 if scales else 0
+    return kv + sc + 2 * q_numel * q_elem + pages * 4 + len(ctx_np) * 4
 
 
 WORKLOAD_NAMES = {"decode_bf16": "config2_llama3_8b_bf16_gqa_decode",
                   "decode_int8": "config3_int8_kv_decode",
                   "decode_fp32": "fp32_gqa_decode",
                   "longctx": "config5_llama3_70b_longctx_kvhead_sharded"}
+
+
+SUB_DROP = ("metric", "n_gpus", "higher_is_better", "vs_baseline", "data")
+
+
+def bench_default(args, world, rank, local):
+    """The default line: BASELINE config 2 as the headline, with the other BASELINE configs
+    measured in the same run as sub-objects -- config 1 through the legacy symbol, config 3
+    (int8 KV), config 5 (KV heads sharded over the N GPUs, strong scaling) and, at N >= 2,
+    config 4 (prefill ranks push KV blocks to decode ranks over NVLink)."""
+    head = bench_decode(args, world, rank, local, "decode_bf16")
+    subs = {"config1": bench_config1(args, world, rank, local),
+            "decode_int8": bench_decode(args, world, rank, local, "decode_int8"),
+            "longctx": bench_decode(args, world, rank, local, "longctx")}
+    if world >= 2 and world % 2 == 0:
+        subs["migrate"] = bench_migrate(args, world, rank, local, steps=min(args.steps, 20))
+    else:
+        subs["migrate"] = {"skipped": "config 4 needs an even number of GPUs >= 2 "
+                                      "(prefill ranks push to decode ranks)"}
+    if rank != 0:
+        return None
+    for name, sub in subs.items():
+        head[name] = {k: v for k, v in sub.items() if k not in SUB_DROP}
+    return head
 
 
 def main():
@@ -1140,16 +1282,20 @@ def main():
         return
     world, rank, local = dist_setup(args)
     try:
-        if args.workload == "migrate":
-            bench_migrate(args, world, rank, local)
+        if args.workload == "default":
+            line = bench_default(args, world, rank, local)
+        elif args.workload == "migrate":
+            line = bench_migrate(args, world, rank, local)
         elif args.workload == "config1":
-            bench_config1(args, world, rank, local)
+            line = bench_config1(args, world, rank, local)
         elif args.workload in ("prefill", "prefill_int8"):
-            bench_prefill(args, world, rank, local)
+            line = bench_prefill(args, world, rank, local)
         elif args.workload == "cow":
-            bench_cow(args, world, rank, local)
+            line = bench_cow(args, world, rank, local)
         else:
-            bench_decode(args, world, rank, local)
+            line = bench_decode(args, world, rank, local)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist
