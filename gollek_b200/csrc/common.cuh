@@ -73,10 +73,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase of `bar` with the given parity.  Returns false (and
-// raises GOLLEK_STATUS_TIMEOUT) if it gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (unsigned i = 0; i < kWaitLimit; ++i)
+// Bounded wait for the phase of `bar` with the given parity (at most `limit` try_waits).
+// Returns false (and raises GOLLEK_STATUS_TIMEOUT) if it gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned limit = kWaitLimit) {
+    for (unsigned i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     raise_status(GOLLEK_STATUS_TIMEOUT);
     return false;

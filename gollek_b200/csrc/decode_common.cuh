@@ -56,6 +56,9 @@ struct DecodeArgs {
     float soft_cap;       // > 0: cap*tanh(score/cap)
     float post_scale;     // log2(e) with soft-cap, else 1
     float norm_eps;       // 1e-9 (engine path) or 0 (legacy fp32 path)
+    unsigned wait_limit;  // bounded waits: try_waits / polls before giving up (0: the default)
+    int fault_skip_group; // test only (-1 = off): CTA 0's producer never issues this CTA-local
+                          // group, so the consumer's bounded wait for it gives up
 };
 
 __host__ __device__ inline uint32_t align_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }

@@ -239,6 +239,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     const int Hkv = a.num_kv_heads;
     const int NS = a.num_stages;
     const int SPW = NS / NC;
+    const unsigned wait_limit = a.wait_limit ? a.wait_limit : kWaitLimit;
+    const unsigned poll_limit = a.wait_limit ? a.wait_limit : kPollLimit;
     auto stage_of = [&](int gi) { return (gi % NC) * SPW + (gi / NC) % SPW; };
     auto round_of = [&](int gi) { return (gi / NC) / SPW; };
 
@@ -277,7 +279,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         const int npg = ROWS / R;                                 // pages per stage (<= 2)
         const int W = NS < GK_WAVE ? NS : GK_WAVE;  // groups per producer wave
         struct GroupLoc {
-            int h, t0, row_off, pid0, pid1, stage, round, len, win_start;
+            int h, t0, row_off, pid0, pid1, stage, round, len, win_start, gi;
             unsigned loaded;
             float ks[2], vs[2];  // per-page int8 scales of the group's pages
         };
@@ -290,6 +292,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             q.h = r.h;
             q.stage = stage_of(gi);
             q.round = round_of(gi);
+            q.gi = gi;
             q.t0 = (q.win_start / ROWS + r.g) * ROWS;
             const int p_first = q.t0 / a.block_size;
             q.row_off = a.block_size < ROWS ? 0 : q.t0 % a.block_size;
@@ -336,6 +339,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         };
         // one group's copies into its stage (the stage is free)
         auto issue = [&](const GroupLoc &q) {
+            // test-only fault injection: leave one group's stage unfilled (its consumer's
+            // bounded wait then gives up; nothing else changes)
+            if (a.fault_skip_group >= 0 && blockIdx.x == 0 && q.gi == a.fault_skip_group) return;
             const int stage = q.stage;
             const int pid0 = checked(q.pid0), pid1 = checked(q.pid1);
             const unsigned loaded = q.loaded;
@@ -401,6 +407,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         };
         int gbase = 0;
         bool aborted = false;
+        int abort_wave = 0;         // first group of the wave that gave up
+        unsigned abort_pending = 0; // its lanes whose group was never issued
         long long xw = x_beg;
         int nw = static_cast<int>(min(static_cast<long long>(W), x_end - xw));
         // cur: this wave (ids and scales ready); nxt: next wave (ids ready, scales in
@@ -430,7 +438,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     pending = false;
                 }
                 if (!__any_sync(0xffffffffu, pending)) break;
-                if (spins > kPollLimit) {
+                if (spins > poll_limit) {
                     if (pending) {
                         raise_status(GOLLEK_STATUS_TIMEOUT);
                         ok = false;
@@ -441,6 +449,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 __nanosleep(GK_POLL_SLEEP_NS);
 #endif
             }
+            const unsigned pend = __ballot_sync(0xffffffffu, pending);
+            const int wave_first = gbase;
             xw = xn;
             gbase = gn;
             nw = nw_next;
@@ -451,15 +461,24 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             nxt = nn;
             if (!__all_sync(0xffffffffu, ok)) {
                 aborted = true;
+                abort_wave = wave_first;
+                abort_pending = pend;
                 break;
             }
         }
-        if (aborted) {
-            // Let every copy already issued land before the CTA's shared memory is released.
+        // Let every copy already issued land before the CTA's shared memory is released:
+        // consumers that gave up (their own wait, or another warp's) skip their stages, so
+        // the last copy into each stage may still be in flight.  Stage s's last issued
+        // group is among the last NS groups -- or, for a lane of the wave that gave up
+        // before issuing, the group NS before it in the same stage (waiting on the
+        // unissued group's phase would alias that copy's predecessor phase).  In a normal
+        // run every such phase has completed and each wait returns at once.
+        {
             const int k = lane;
             if (k < NS && k < gbase) {
-                const int g = gbase - 1 - k;
-                mbar_wait(&full_bar[stage_of(g)], round_of(g) & 1);
+                int g = gbase - 1 - k;
+                if (aborted && g >= abort_wave && ((abort_pending >> (g - abort_wave)) & 1u)) g -= NS;
+                if (g >= 0) mbar_wait(&full_bar[stage_of(g)], round_of(g) & 1, wait_limit);
             }
         }
         return;
@@ -614,7 +633,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (*cons_abort) continue;
                 const int stage = warp * SPW + my_slot;
                 bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase);
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (++my_slot == SPW) {
                     my_slot = 0;
@@ -935,7 +954,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (*cons_abort) continue;
                 const int stage = warp * SPW + my_slot;
                 bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase);
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (++my_slot == SPW) {
                     my_slot = 0;
@@ -1178,7 +1197,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (*cons_abort) continue;
                 const int stage = warp * SPW + my_slot;
                 bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase);
+                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (++my_slot == SPW) {
                     my_slot = 0;
@@ -1436,6 +1455,10 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
                 if (tid == 0) atomicExch(&a.counters[r.s * Hkv + r.h], 0);
             }
+        } else {
+            // Every thread has read the warp states of this run before any warp writes
+            // the next run's (a warp with no group in the next run gets there quickly).
+            named_barrier(1, CONS);
         }
     }
 }

@@ -473,6 +473,12 @@ DecodeArgs v2_args(const V2 &p, void *ws, size_t ws_cap, long long page_stride, 
     a.soft_cap = p.soft_cap;
     a.post_scale = cap ? kLog2e : 1.f;
     a.norm_eps = p.norm_eps;
+    // Test hooks of the failure-detection tests (unset in normal use): a short bound for the
+    // kernels' waits, and one group of CTA 0 whose copies are never issued.
+    const char *wl = std::getenv("GOLLEK_TEST_WAIT_LIMIT");
+    const char *sk = std::getenv("GOLLEK_TEST_SKIP_GROUP");
+    a.wait_limit = wl ? static_cast<unsigned>(std::strtoul(wl, nullptr, 10)) : 0u;
+    a.fault_skip_group = sk ? std::atoi(sk) : -1;
     return a;
 }
 

@@ -8,8 +8,10 @@ engine/generation/:
   attention/PagedAttentionVectorAPI.compute -> paged_attention_compute (gollek_paged_attention_v2)
 
 FP32, INT8 and INT4 storage follow the reference bit for bit on the write side (per
-(block, head, token) symmetric scales); BF16 storage is an extension.  Decode only: a query
-of one token per sequence (multi-token prefill attention is not part of this path).
+(block, head, token) symmetric scales); BF16 storage is an extension.  A call with one
+query token per sequence runs decode attention (gollek_paged_attention_v2); with Tq > 1 new
+tokens (a prefill chunk, speculative verification) it runs multi-query attention
+(gollek_paged_attention_prefill), causal by default, like compute with seqLenQ > 1.
 """
 from __future__ import annotations
 

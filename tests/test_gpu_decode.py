@@ -442,6 +442,56 @@ def test_int8_window_and_softcap(cuda_device, window, soft_cap):
     np.testing.assert_allclose(got.float().cpu().numpy(), want, atol=2e-2, rtol=0)
 
 
+@pytest.mark.parametrize("hq", [8, 16, 32, 64])
+@pytest.mark.parametrize("per_token", [True, False])
+def test_int8_long_contexts_split_k(cuda_device, hq, per_token):
+    """GQA 1/2/4/8 over contexts long enough that (sequence, kv-head) pairs are cut into
+    split-K pieces, a few sequences only (many pieces each), both scale granularities."""
+    ctx = [9000, 31, 4097, 12000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=8, d=128, bs=16, seed=29 + hq, kv_std=0.5)
+    qb = O.round_bf16(q)
+    if per_token:
+        kq, ks = quantize_rows_int8(k)
+        vq, vs = quantize_rows_int8(v)
+        strides, ks_t, vs_t = (8 * 16, 16, 1), ks, vs
+    else:
+        kq, ks = quantize_pages_int8(O.round_bf16(k))
+        vq, vs = quantize_pages_int8(O.round_bf16(v))
+        strides = (8, 1, 0)
+        ks_t = np.repeat(ks[:, :, None], 16, axis=2)
+        vs_t = np.repeat(vs[:, :, None], 16, axis=2)
+    want = oracle_decode(qb, kq, vq, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16, storage=O.INT8,
+                         k_scale=ks_t, v_scale=vs_t)
+    got = _int8_call(cuda_device, qb, kq, vq, bt, ctx, ks, vs, strides, q_dtype=torch.bfloat16)
+    from gollek_b200 import ops
+    assert ops.device_status(cuda_device.index, clear=True) == 0
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
+def test_int8_stale_table_entries_outside_the_window(cuda_device):
+    """Pages wholly before a sliding window, and the page after a context's last token, may
+    hold stale table entries (-1 here): they must be neither read nor reported."""
+    from gollek_b200 import ops
+    ctx = [200, 333, 1000]
+    q, k, v, bt, ctx = decode_case(ctx, hq=32, hkv=8, d=128, bs=16, seed=41, kv_std=0.5)
+    kq, ks = quantize_rows_int8(k)
+    vq, vs = quantize_rows_int8(v)
+    qb = O.round_bf16(q)
+    window = 100
+    bt2 = bt.copy()
+    for s_, c in enumerate(ctx):
+        first = (int(c) - window) // 16  # first page holding a token of the window
+        bt2[s_, :max(0, first)] = -1
+        bt2[s_, (int(c) + 15) // 16:] = -1
+    want = oracle_decode(qb, kq, vq, bt, ctx, 1 / math.sqrt(128), hkv=8, bs=16, storage=O.INT8,
+                         k_scale=ks, v_scale=vs, window=window)
+    ops.device_status(cuda_device.index, clear=True)
+    got = _int8_call(cuda_device, qb, kq, vq, bt2, ctx, ks, vs, (8 * 16, 16, 1), window=window,
+                     q_dtype=torch.bfloat16)
+    assert ops.device_status(cuda_device.index, clear=True) == 0
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, atol=2e-2, rtol=0)
+
+
 # ------------------------------------------------------------------ both 16-bit kernels
 
 _PATH_CASES = [
