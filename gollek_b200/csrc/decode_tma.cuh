@@ -865,21 +865,40 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             // g is dim 16g+2mt and row g+8 is dim 16g+2mt+1.
             // A group of ROWS tokens is NT score n-tiles of 8 tokens and VK value k-steps
             // of 16 tokens; 16-token groups keep two accumulator chains per n-tile.
+            // Token sets (SETS = 2, GQA groups of <= 4 rows, q unsplit): the 8 MMA rows hold
+            // the G rows twice -- rows [0, G) against the even 8-token n-tiles, rows
+            // [G, 2G) against the odd ones -- by stacking the two n-tiles' K along the
+            // MMA's k dimension with each row's q zero over the other set's k-steps.  A
+            // score MMA then yields 2G useful rows instead of G, so every lane's
+            // accumulators hold live scores and the online softmax does half the work per
+            // lane; the value MMA takes the odd set's probabilities by one shuffle.
             constexpr int KS = D / 16;
             constexpr int NT = ROWS / 8;
             constexpr int VK = ROWS / 16;
             constexpr int CH = NT >= 4 ? 1 : 2;
+            constexpr int SETS = (G <= 4 && !SPLIT) ? 2 : 1;
+            constexpr int NTC = NT / SETS;  // score accumulator tiles (8 * SETS tokens each)
+            constexpr int RU = G * SETS;    // MMA rows in use
             static_assert(D == 128, "int8 tensor-pipe path: head_dim 128");
+            static_assert(NT % SETS == 0 && VK == NTC * SETS / 2, "token-set tiling");
             const int g = lane >> 2;
             const int t = lane & 3;
+            const int gm = g % G;                 // row of the model (head or folded query row)
+            const int myset = (g / G) % SETS;     // the n-tiles this lane's row scores
+            const bool row_used = g < RU;
             const int R = a.block_size < ROWS ? a.block_size : ROWS;
             uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
+            // the A operand of set js: this lane's q on its own set's k-steps, zero on the
+            // other's (one AND per register as the MMAs are issued)
+            uint32_t qmask[SETS];
+#pragma unroll
+            for (int js = 0; js < SETS; ++js) qmask[js] = myset == js ? 0xffffffffu : 0u;
             float qmul;         // score multiplier: q_scale times the power of two taken out of q
             float qsum = 0.f;   // head g's sum of the f16 q values the MMAs see
             {
                 float qf[32];
-                const long long qrow = qo_row(r.s, r.h, g < G ? g : 0, Hkv, G, a.qfold, a.seq_div) * D + 32 * t;
-                if (g < G) {
+                const long long qrow = qo_row(r.s, r.h, row_used ? gm : 0, Hkv, G, a.qfold, a.seq_div) * D + 32 * t;
+                if (row_used) {
                     if (a.q_bf16) {
                         const uint4 *src = reinterpret_cast<const uint4 *>(
                             reinterpret_cast<const __nv_bfloat16 *>(a.q) + qrow);
@@ -926,8 +945,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     for (int hf = 0; hf < 2; ++hf) {
                         const float x0 = qf[4 * kk + 2 * hf] * down;
                         const float x1 = qf[4 * kk + 2 * hf + 1] * down;
-                        qa[kk][hf] = pack2<__half>(x0, x1);
-                        const float2 back = unpack2<__half>(qa[kk][hf]);
+                        const uint32_t qh = pack2<__half>(x0, x1);
+                        qa[kk][hf] = qh;
+                        const float2 back = unpack2<__half>(qh);
                         qsum += back.x + back.y;
                         if constexpr (SPLIT) {
                             ql[kk][hf] = pack2<__half>(x0 - back.x, x1 - back.y);
@@ -943,7 +963,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float l_run = 0.f;        // this lane's share of head g's normaliser
             float ps_run = 0.f;       // this lane's share of head g's probability mass in o
             // folded multi-query rows: row g's query sees the positions before len - qshift
-            const int qshift = (a.qfold > 1 && g < G) ? a.qfold - 1 - g / (G / a.qfold) : 0;
+            const int qshift = (a.qfold > 1 && row_used) ? a.qfold - 1 - gm / (G / a.qfold) : 0;
             int ev = 0;               // o holds O * 2^-ev
             bool ev_set = false;
             float o[KS][4];
@@ -979,47 +999,60 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                     for (int hf = 0; hf < 2; ++hf)
                         kr[nt][hf] = lds_u4(kt + swz<ROWS>(g + 8 * nt, 32 * t + 16 * hf));
                 const uint32_t sc = smem_u32(sm_scale) + static_cast<uint32_t>(stage) * 2 * ROWS * 4;
-                // scales of tokens 8nt + 2t + e: one per page (slot = token / R), or per token
+                // scales of this lane's tokens 8nt + 2t + e (nt = nc * SETS + myset): one per
+                // page (slot = token / R), or per token
                 auto read_scales = [&](float (*dst)[2], uint32_t base) {
                     if (a.scale_mode == 1) {
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt) {
+                        for (int nc = 0; nc < NTC; ++nc) {
+                            const int nt = nc * SETS + myset;
                             float f;
                             asm volatile("ld.shared.f32 %0, [%1];"
                                          : "=f"(f)
                                          : "r"(base + static_cast<uint32_t>((8 * nt) / R) * 4));
-                            dst[nt][0] = dst[nt][1] = f;
+                            dst[nc][0] = dst[nc][1] = f;
                         }
                     } else {  // tokens 2t, 2t+1 of each n-tile are adjacent
 #pragma unroll
-                        for (int nt = 0; nt < NT; ++nt) {
+                        for (int nc = 0; nc < NTC; ++nc) {
+                            const int nt = nc * SETS + myset;
                             const uint2 w2 = lds_u2(base + (8 * nt + 2 * t) * 4);
-                            dst[nt][0] = __uint_as_float(w2.x);
-                            dst[nt][1] = __uint_as_float(w2.y);
+                            dst[nc][0] = __uint_as_float(w2.x);
+                            dst[nc][1] = __uint_as_float(w2.y);
                         }
                     }
                 };
-                float ksc[NT][2], vsc[NT][2];
+                float ksc[NTC][2], vsc[NTC][2];
                 read_scales(ksc, sc);
                 // ---------------- scores
-                float s[CH][NT][4];
+                float s[CH][NTC][4];
 #pragma unroll
                 for (int c = 0; c < CH; ++c)
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+                    for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) s[c][nt][e] = 0.f;
+                        for (int e = 0; e < 4; ++e) s[c][nc][e] = 0.f;
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
                     float(*acc)[4] = s[kk % CH];
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        const uint4 &q4 = kr[nt][kk >> 2];
-                        const uint32_t w = (kk & 3) == 0 ? q4.x : (kk & 3) == 1 ? q4.y : (kk & 3) == 2 ? q4.z : q4.w;
-                        uint32_t b0, b1;
-                        i8x4_to_f16x2_biased(w, b0, b1);
-                        mma_16816<__half>(acc[nt], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
-                        if constexpr (SPLIT) mma_16816<__half>(acc[nt], ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
+                    for (int js = 0; js < SETS; ++js) {
+                        // (volatile: keep the AND here -- hoisted out of the group loop, the
+                        // masked copies would need 16 more registers than the budget has)
+                        uint32_t a0 = qa[kk][0], a2 = qa[kk][1];
+                        if constexpr (SETS == 2) {
+                            asm volatile("and.b32 %0, %0, %1;" : "+r"(a0) : "r"(qmask[js]));
+                            asm volatile("and.b32 %0, %0, %1;" : "+r"(a2) : "r"(qmask[js]));
+                        }
+#pragma unroll
+                        for (int nc = 0; nc < NTC; ++nc) {
+                            const uint4 &q4 = kr[nc * SETS + js][kk >> 2];
+                            const uint32_t w = (kk & 3) == 0 ? q4.x : (kk & 3) == 1 ? q4.y : (kk & 3) == 2 ? q4.z : q4.w;
+                            uint32_t b0, b1;
+                            i8x4_to_f16x2_biased(w, b0, b1);
+                            mma_16816<__half>(acc[nc], a0, 0u, a2, 0u, b0, b1);
+                            if constexpr (SPLIT) mma_16816<__half>(acc[nc], ql[kk][0], 0u, ql[kk][1], 0u, b0, b1);
+                        }
                     }
                 }
                 // ---------------- V words and scales to registers, then free the stage
@@ -1034,39 +1067,45 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 if (lane == 0) mbar_arrive(&empty_bar[stage]);
                 if constexpr (CH == 2) {
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+                    for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
-                        for (int e = 0; e < 2; ++e) s[0][nt][e] += s[1][nt][e];
+                        for (int e = 0; e < 2; ++e) s[0][nc][e] += s[1][nc][e];
                 }
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
-                    for (int e = 0; e < 2; ++e) s[0][nt][e] -= qbias;
+                    for (int e = 0; e < 2; ++e) s[0][nc][e] -= qbias;
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
                 // (vmax spans the group's window, the same for every row, so the V-scale
                 // exponent stays warp-uniform; row g's own causal bound masks its scores)
                 const int row_hi = min(v_hi, sw.len - qshift - t0);
-                float p[NT][2];
-                bool valid[NT][2];
+                float p[NTC][2];
+                bool valid[NTC][2];
                 float mloc = -INFINITY;
                 float vmax = 0.f;
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
-                        const int tk = 8 * nt + 2 * t + e;
-                        if (tk >= v_lo && tk < v_hi) vmax = fmaxf(vmax, vsc[nt][e]);
-                        valid[nt][e] = tk >= v_lo && tk < row_hi;
-                        float x2 = s[0][nt][e] * qmul * ksc[nt][e];
+                        const int tk = 8 * (nc * SETS + myset) + 2 * t + e;
+                        if (tk >= v_lo && tk < v_hi) vmax = fmaxf(vmax, vsc[nc][e]);
+                        valid[nc][e] = row_used && tk >= v_lo && tk < row_hi;
+                        float x2 = s[0][nc][e] * qmul * ksc[nc][e];
                         if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
-                        x2 = valid[nt][e] ? x2 : -INFINITY;
-                        p[nt][e] = x2;
+                        x2 = valid[nc][e] ? x2 : -INFINITY;
+                        p[nc][e] = x2;
                         mloc = fmaxf(mloc, x2);
                     }
+                // reduce over the quad's tokens and, with two sets, over the other set's
+                // row of the same head (lane + or - 4G): every (row, head) pair then agrees
                 mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
                 mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
                 vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
                 vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+                if constexpr (SETS == 2) {
+                    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 4 * G));
+                    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4 * G));
+                }
                 const float mn = fmaxf(m_run, mloc);
                 const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
                 const float mref = (mn == -INFINITY) ? 0.f : mn;
@@ -1079,24 +1118,26 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
                 const float vmul = pow2i(-ev_new);
                 float psum = 0.f;
-                float pv[NT][2];
+                float pv[NTC][2];
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
-                        const float pe = fast_exp2(p[nt][e] - mref);
+                        const float pe = fast_exp2(p[nc][e] - mref);
                         psum += pe;
-                        pv[nt][e] = valid[nt][e] ? pe * (vsc[nt][e] * vmul) : 0.f;
+                        pv[nc][e] = valid[nc][e] ? pe * (vsc[nc][e] * vmul) : 0.f;
                     }
                 l_run = l_run * alpha + psum;
                 // probabilities as the value MMA's B fragments: n-tile nt holds tokens
                 // 8nt + 2t, 8nt + 2t + 1 of head g, i.e. k rows 2t, 2t+1 (+8) of k-step nt / 2
-                uint32_t pb[NT];
+                // (two sets: this lane holds n-tile 2nc + myset; the odd one comes from the
+                // lane 4G above)
+                uint32_t pb[NTC];
                 float pmass = 0.f;
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    pb[nt] = pack2<__half>(pv[nt][0], pv[nt][1]);
-                    const float2 pr = unpack2<__half>(pb[nt]);
+                for (int nc = 0; nc < NTC; ++nc) {
+                    pb[nc] = pack2<__half>(pv[nc][0], pv[nc][1]);
+                    const float2 pr = unpack2<__half>(pb[nc]);
                     pmass += pr.x + pr.y;
                 }
                 const float fac = ev_set ? alpha * pow2i(max(-126, min(127, ev - ev_new))) : alpha;
@@ -1117,6 +1158,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 // ---------------- values: per k-step, rows 2t, 2t+1 (a0, a1) and 2t+8, 2t+9 (a2, a3)
 #pragma unroll
                 for (int vk = 0; vk < VK; ++vk) {
+                    uint32_t pb0, pb1;
+                    if constexpr (SETS == 2) {
+                        pb0 = pb[vk];
+                        pb1 = __shfl_down_sync(0xffffffffu, pb[vk], 4 * G);
+                    } else {
+                        pb0 = pb[2 * vk];
+                        pb1 = pb[2 * vk + 1];
+                    }
 #pragma unroll
                     for (int w = 0; w < 4; ++w) {
                         const uint4 *v4 = vr[vk];
@@ -1129,8 +1178,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         i8x4_to_f16x2_biased(__byte_perm(ra, rb, 0x7362), a0o, a1o);  // dims 4w+2, 4w+3
                         i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x5140), a2e, a3e);
                         i8x4_to_f16x2_biased(__byte_perm(rc, rd, 0x7362), a2o, a3o);
-                        mma_16816<__half>(o[2 * w], a0e, a1e, a2e, a3e, pb[2 * vk], pb[2 * vk + 1]);
-                        mma_16816<__half>(o[2 * w + 1], a0o, a1o, a2o, a3o, pb[2 * vk], pb[2 * vk + 1]);
+                        mma_16816<__half>(o[2 * w], a0e, a1e, a2e, a3e, pb0, pb1);
+                        mma_16816<__half>(o[2 * w + 1], a0o, a1o, a2o, a3o, pb0, pb1);
                     }
                 }
             }
@@ -1140,6 +1189,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float *cw = sm_comb + warp * G * (D + 2);
             l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
             l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+            if constexpr (SETS == 2) l_run += __shfl_xor_sync(0xffffffffu, l_run, 4 * G);
             if (t == 0 && g < G) {
                 cw[g] = m_run;
                 cw[G + g] = l_run;
@@ -1147,6 +1197,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             // the biased V bytes added 1152 times each head's probability mass to o
             ps_run += __shfl_xor_sync(0xffffffffu, ps_run, 1);
             ps_run += __shfl_xor_sync(0xffffffffu, ps_run, 2);
+            if constexpr (SETS == 2) ps_run += __shfl_xor_sync(0xffffffffu, ps_run, 4 * G);
             const float bias0 = 1152.f * __shfl_sync(0xffffffffu, ps_run, 8 * t);      // head 2t
             const float bias1 = 1152.f * __shfl_sync(0xffffffffu, ps_run, 8 * t + 4);  // head 2t+1
             const float om = pow2i(ev);
