@@ -58,6 +58,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--gather", action="store_true", help="longctx: all-gather head-sharded outputs")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="with --workload: sequences per batch instead of the BASELINE config's "
+                         "(a smaller case for profiling; the line's config reports it)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -86,10 +89,16 @@ def traffic_per_launch(workload):
 
 # ------------------------------------------------------------------ workloads
 
+BATCH_OVERRIDE = {}  # workload -> sequences (--seqs: smaller cases for ncu captures)
+
+
 def decode_shape(workload):
     if workload == "longctx":
-        return dict(hq=64, hkv=8, d=128, bs=16, batch=256, lo=4096, hi=131072, dist="loguniform")
-    return dict(hq=32, hkv=8, d=128, bs=16, batch=64, lo=512, hi=8192, dist="uniform")
+        sh = dict(hq=64, hkv=8, d=128, bs=16, batch=256, lo=4096, hi=131072, dist="loguniform")
+    else:
+        sh = dict(hq=32, hkv=8, d=128, bs=16, batch=64, lo=512, hi=8192, dist="uniform")
+    sh["batch"] = BATCH_OVERRIDE.get(workload, sh["batch"])
+    return sh
 
 
 def context_lengths(shape, rng):
@@ -1280,6 +1289,8 @@ def main():
     if args.impl == "reference":
         bench_reference(args)
         return
+    if args.seqs > 0 and args.workload != "default":
+        BATCH_OVERRIDE[args.workload] = args.seqs
     world, rank, local = dist_setup(args)
     try:
         if args.workload == "default":
