@@ -189,16 +189,25 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int kv_bytes, bool quan
 // SPLIT (tensor-pipe consumers): q is wider than the MMA type (fp32 q, or any q with
 // f16 KV or int8 KV) and enters the score MMA as hi + lo halves.  ROWS: tokens per
 // group and stage (32 only for int8 KV; the launch sets DecodeArgs::group_rows to it).
-template <typename KV, int D, int G, int NC, bool SPLIT, int ROWS = kRows>
+// PAIR (int8, 16-token pages, 32-token groups): the unit is a (sequence, kv-head pair) and a
+// stage holds both heads of each page -- one 4 KB TMA box per page instead of two 2 KB ones
+// (the copy path's rate is set by boxes, not bytes, for boxes this small).  Consumer warps
+// 2i and 2i+1 share stage ring i, each computing one head of the pair over the same groups;
+// a unit's output rows are its two heads' G rows each (a.num_kv_heads counts pairs).
+template <typename KV, int D, int G, int NC, bool SPLIT, int ROWS = kRows, bool PAIR = false>
 __global__ void __launch_bounds__((NC + 1) * 32, 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const DecodeArgs a) {
     constexpr int KB = KvType<KV>::kBytes;
     constexpr bool QUANT = KvType<KV>::kQuant;
     constexpr bool I8MMA = std::is_same<KV, int8_t>::value && D == 128;  // int8 on the tensor pipe
+    constexpr int HP = PAIR ? 2 : 1;         // kv-heads per unit and stage
+    constexpr int UG = G * HP;               // output rows per unit
+    constexpr int NP = NC / HP;              // stage-ring owners (warp pairs in PAIR mode)
+    constexpr int TROWS = ROWS * HP;         // rows of one K (or V) stage tile
     constexpr int ROW_BYTES = D * KB;
     constexpr int NSLAB = ROW_BYTES / 128;
-    constexpr int SLAB = ROWS * 128;         // bytes of one 128-byte column slab
+    constexpr int SLAB = TROWS * 128;        // bytes of one 128-byte column slab
     constexpr int TILE = NSLAB * SLAB;
     constexpr int HALF_CH = ROW_BYTES / 32;  // 16-byte chunks per head-dim half
     constexpr int EPC = 16 / KB;             // elements per chunk
@@ -212,13 +221,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     static_assert(EPL % 2 == 0 && EPC % 4 == 0 && D % 64 == 0, "vector widths");
     static_assert(NSLAB * 2 * 2 <= 32, "TMA loads of one stage (<= 2 pages) fit a warp");
     static_assert(ROWS == kRows || (I8MMA && ROWS == 32), "32-token groups: int8 KV only");
+    static_assert(!PAIR || (I8MMA && ROWS == 32 && NC % 2 == 0 && !SPLIT), "pairs: int8, 32-token groups");
 
     extern __shared__ __align__(16) uint8_t smem_raw[];
     // Align to 1024 bytes by pointer arithmetic on the shared array (keeps the
     // shared address space visible to the compiler).
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const DecodeSmem L =
-        decode_smem_layout(KB, QUANT, D, G, NC, a.num_stages, a.num_seqs, gridDim.x, ROWS);
+        decode_smem_layout(KB, QUANT, D, G, NC, a.num_stages, a.num_seqs, gridDim.x, TROWS);
     uint8_t *sm_stage = smem + L.stages;
     float *sm_q = reinterpret_cast<float *>(smem + L.q);
     float *sm_p = reinterpret_cast<float *>(smem + L.p);
@@ -238,17 +248,17 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     const int S = a.num_seqs;
     const int Hkv = a.num_kv_heads;
     const int NS = a.num_stages;
-    const int SPW = NS / NC;
+    const int SPW = NS / NP;
     const unsigned wait_limit = a.wait_limit ? a.wait_limit : kWaitLimit;
     const unsigned poll_limit = a.wait_limit ? a.wait_limit : kPollLimit;
-    auto stage_of = [&](int gi) { return (gi % NC) * SPW + (gi / NC) % SPW; };
-    auto round_of = [&](int gi) { return (gi / NC) / SPW; };
+    auto stage_of = [&](int gi) { return (gi % NP) * SPW + (gi / NP) % SPW; };
+    auto round_of = [&](int gi) { return (gi / NP) / SPW; };
 
     // ------------------------------------------------------------ prologue
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(&full_bar[i], (QUANT && a.scale_mode == 2) ? 2 : 1);
-            mbar_init(&empty_bar[i], 1);
+            mbar_init(&empty_bar[i], HP);  // every warp of the ring's owner releases
         }
         fence_barrier_init();
         sm_misc[0] = 0;  // "this CTA merges the partials" flag
@@ -275,13 +285,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
         // stage to be free and issues its own TMA loads, without waiting for the other
         // lanes.  The next wave's page ids are looked up (block-table loads in flight)
         // while the current wave waits and issues, so a wave starts with its ids ready.
-        const int R = a.block_size < ROWS ? a.block_size : ROWS;  // rows per TMA box
+        const int R = a.block_size < ROWS ? a.block_size : ROWS;  // token rows of a page in a group
         const int npg = ROWS / R;                                 // pages per stage (<= 2)
+        const int RB = R * HP;                                    // rows per TMA box (both heads)
         const int W = NS < GK_WAVE ? NS : GK_WAVE;  // groups per producer wave
         struct GroupLoc {
             int h, t0, row_off, pid0, pid1, stage, round, len, win_start, gi;
             unsigned loaded;
-            float ks[2], vs[2];  // per-page int8 scales of the group's pages
+            float ks[2 * HP], vs[2 * HP];  // per-(page, head) int8 scales of the group's pages
         };
         auto locate_group = [&](long long x, int gi) {
             GroupLoc q;
@@ -329,11 +340,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                     if (j >= npg || !((q.loaded >> j) & 1)) continue;
-                    const long long so =
-                        static_cast<long long>(checked(j ? q.pid1 : q.pid0)) * a.scale_page_stride +
-                        static_cast<long long>(q.h) * a.scale_head_stride;
-                    q.ks[j] = __ldg(a.k_scales + so);
-                    q.vs[j] = __ldg(a.v_scales + so);
+#pragma unroll
+                    for (int hh = 0; hh < HP; ++hh) {
+                        const long long so =
+                            static_cast<long long>(checked(j ? q.pid1 : q.pid0)) * a.scale_page_stride +
+                            static_cast<long long>(q.h * HP + hh) * a.scale_head_stride;
+                        q.ks[j * HP + hh] = __ldg(a.k_scales + so);
+                        q.vs[j * HP + hh] = __ldg(a.v_scales + so);
+                    }
                 }
             }
         };
@@ -348,23 +362,26 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             uint8_t *kdst = sm_stage + static_cast<uint32_t>(stage) * 2 * TILE;
             uint8_t *vdst = kdst + TILE;
             if constexpr (QUANT) {
-                if (page_scales) {
-                    float *ks = sm_scale + stage * 2 * ROWS;
+                if (page_scales) {  // slot j * HP + hh: page j, head hh of the unit
+                    float *ks = sm_scale + stage * 2 * TROWS;
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         if (j >= npg || !((loaded >> j) & 1)) continue;
-                        ks[j] = q.ks[j];
-                        ks[ROWS + j] = q.vs[j];
+#pragma unroll
+                        for (int hh = 0; hh < HP; ++hh) {
+                            ks[j * HP + hh] = q.ks[j * HP + hh];
+                            ks[TROWS + j * HP + hh] = q.vs[j * HP + hh];
+                        }
                     }
                 }
             }
-            const uint32_t scale_tx = (QUANT && a.scale_mode == 0) ? 2u * R * 4u : 0u;
+            const uint32_t scale_tx = (QUANT && a.scale_mode == 0) ? 2u * RB * 4u : 0u;
             mbar_arrive_expect_tx(&full_bar[stage], static_cast<uint32_t>(__popc(loaded)) *
-                                                        (2u * NSLAB * R * 128u + scale_tx));
+                                                        (2u * NSLAB * RB * 128u + scale_tx));
             for (int j = 0; j < npg; ++j) {
                 if (!((loaded >> j) & 1)) continue;
                 const long long y = static_cast<long long>(j ? pid1 : pid0) * a.page_rows +
-                                    static_cast<long long>(q.h) * a.block_size + q.row_off;
+                                    static_cast<long long>(q.h) * HP * a.block_size + q.row_off;
                 if (a.box3d) {  // ROWS rows x all slabs in one box each for K and V
                     tma_load_3d(kdst, &tm_k, 0, static_cast<int>(y), 0, &full_bar[stage]);
                     tma_load_3d(vdst, &tm_v, 0, static_cast<int>(y), 0, &full_bar[stage]);
@@ -372,22 +389,23 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 }
 #pragma unroll
                 for (int slab = 0; slab < NSLAB; ++slab) {
-                    tma_load_2d(kdst + slab * SLAB + j * R * 128, &tm_k, slab * (128 / KB),
+                    tma_load_2d(kdst + slab * SLAB + j * RB * 128, &tm_k, slab * (128 / KB),
                                 static_cast<int>(y), &full_bar[stage]);
-                    tma_load_2d(vdst + slab * SLAB + j * R * 128, &tm_v, slab * (128 / KB),
+                    tma_load_2d(vdst + slab * SLAB + j * RB * 128, &tm_v, slab * (128 / KB),
                                 static_cast<int>(y), &full_bar[stage]);
                 }
             }
             if constexpr (QUANT) {
-                float *ks = sm_scale + stage * 2 * ROWS;
+                float *ks = sm_scale + stage * 2 * TROWS;
                 if (a.scale_mode == 0) {
-                    // per-token scales: R contiguous floats per page, one bulk copy each
+                    // per-token scales: R contiguous floats per page and head (RB for the two
+                    // heads of a pair, adjacent when the head stride is R), one bulk copy each
                     for (int j = 0; j < npg; ++j) {
                         if (!((loaded >> j) & 1)) continue;
                         const long long so = static_cast<long long>(j ? pid1 : pid0) * a.scale_page_stride +
-                                             static_cast<long long>(q.h) * a.scale_head_stride + q.row_off;
-                        bulk_load(ks + j * R, a.k_scales + so, R * 4u, &full_bar[stage]);
-                        bulk_load(ks + ROWS + j * R, a.v_scales + so, R * 4u, &full_bar[stage]);
+                                             static_cast<long long>(q.h) * HP * a.scale_head_stride + q.row_off;
+                        bulk_load(ks + j * RB, a.k_scales + so, RB * 4u, &full_bar[stage]);
+                        bulk_load(ks + TROWS + j * RB, a.v_scales + so, RB * 4u, &full_bar[stage]);
                     }
                 } else if (a.scale_mode == 2) {
                     for (int tk = 0; tk < ROWS; ++tk) {
@@ -398,7 +416,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                                                  static_cast<long long>(q.h) * a.scale_head_stride +
                                                  static_cast<long long>(t % a.block_size) * a.scale_token_stride;
                             cp_async_4(ks + tk, a.k_scales + so);
-                            cp_async_4(ks + ROWS + tk, a.v_scales + so);
+                            cp_async_4(ks + TROWS + tk, a.v_scales + so);
                         }
                     }
                     cp_async_mbar_arrive_noinc(&full_bar[stage]);
@@ -491,12 +509,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
     const int li = lane & 15;
     const uint32_t p_base = smem_u32(sm_p) + warp * ROWS * GP * 4;
     volatile int *cons_abort = sm_misc + 3;
+    const int ow = warp / HP;  // owner of this warp's stage ring
+    const int hsel = warp % HP;  // PAIR: the head of the pair this warp computes
 
     // Sequences with nothing to attend to: zeros, written by CTA s % grid.
     for (int s = blockIdx.x; s < S; s += gridDim.x) {
         if (sm_prefix[s + 1] != sm_prefix[s]) continue;
-        for (int o = tid; o < Hkv * G * D; o += CONS)
-            store_out(a.out, static_cast<long long>(s) * Hkv * G * D + o, 0.f, a.q_bf16);
+        for (int o = tid; o < Hkv * UG * D; o += CONS)
+            store_out(a.out, static_cast<long long>(s) * Hkv * UG * D + o, 0.f, a.q_bf16);
     }
 
     // bf16 q with bf16 KV: q's words are the score MMA's A fragments as they are, so the
@@ -629,9 +649,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             const int lm_tok = (lane & 7) + 8 * (lane >> 4);
             const int lm_col = 8 * ((lane >> 3) & 1);
 
-            for (int j = ((warp - gidx) % NC + NC) % NC; j < r.len; j += NC) {
+            for (int j = ((ow - gidx) % NP + NP) % NP; j < r.len; j += NP) {
                 if (*cons_abort) continue;
-                const int stage = warp * SPW + my_slot;
+                const int stage = ow * SPW + my_slot;
                 bool ok = true;
                 if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -887,6 +907,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             const int myset = (g / G) % SETS;     // the n-tiles this lane's row scores
             const bool row_used = g < RU;
             const int R = a.block_size < ROWS ? a.block_size : ROWS;
+            // stage row of the group's token tau (PAIR: pages of 16 rows of each head, the
+            // two heads of a page adjacent, so row = 32 * page + 16 * head + slot)
+            auto srow = [&](int tau) { return PAIR ? ((tau >> 4) << 5) + (hsel << 4) + (tau & 15) : tau; };
             uint32_t qa[KS][2], ql[SPLIT ? KS : 1][2];
             // the A operand of set js: this lane's q on its own set's k-steps, zero on the
             // other's (one AND per register as the MMAs are issued)
@@ -897,7 +920,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             float qsum = 0.f;   // head g's sum of the f16 q values the MMAs see
             {
                 float qf[32];
-                const long long qrow = qo_row(r.s, r.h, row_used ? gm : 0, Hkv, G, a.qfold, a.seq_div) * D + 32 * t;
+                const long long qrow =
+                    qo_row(r.s, r.h * HP + hsel, row_used ? gm : 0, Hkv * HP, G, a.qfold, a.seq_div) * D + 32 * t;
                 if (row_used) {
                     if (a.q_bf16) {
                         const uint4 *src = reinterpret_cast<const uint4 *>(
@@ -970,9 +994,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
             for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
-            for (int j = ((warp - gidx) % NC + NC) % NC; j < r.len; j += NC) {
+            for (int j = ((ow - gidx) % NP + NP) % NP; j < r.len; j += NP) {
                 if (*cons_abort) continue;
-                const int stage = warp * SPW + my_slot;
+                const int stage = ow * SPW + my_slot;
                 bool ok = true;
                 if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -997,8 +1021,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int hf = 0; hf < 2; ++hf)
-                        kr[nt][hf] = lds_u4(kt + swz<ROWS>(g + 8 * nt, 32 * t + 16 * hf));
-                const uint32_t sc = smem_u32(sm_scale) + static_cast<uint32_t>(stage) * 2 * ROWS * 4;
+                        kr[nt][hf] = lds_u4(kt + swz<TROWS>(srow(g + 8 * nt), 32 * t + 16 * hf));
+                const uint32_t sc = smem_u32(sm_scale) + static_cast<uint32_t>(stage) * 2 * TROWS * 4;
                 // scales of this lane's tokens 8nt + 2t + e (nt = nc * SETS + myset): one per
                 // page (slot = token / R), or per token
                 auto read_scales = [&](float (*dst)[2], uint32_t base) {
@@ -1009,14 +1033,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                             float f;
                             asm volatile("ld.shared.f32 %0, [%1];"
                                          : "=f"(f)
-                                         : "r"(base + static_cast<uint32_t>((8 * nt) / R) * 4));
+                                         : "r"(base + static_cast<uint32_t>(((8 * nt) / R) * HP + hsel) * 4));
                             dst[nc][0] = dst[nc][1] = f;
                         }
                     } else {  // tokens 2t, 2t+1 of each n-tile are adjacent
 #pragma unroll
                         for (int nc = 0; nc < NTC; ++nc) {
                             const int nt = nc * SETS + myset;
-                            const uint2 w2 = lds_u2(base + (8 * nt + 2 * t) * 4);
+                            const uint2 w2 = lds_u2(base + srow(8 * nt + 2 * t) * 4);
                             dst[nc][0] = __uint_as_float(w2.x);
                             dst[nc][1] = __uint_as_float(w2.y);
                         }
@@ -1061,8 +1085,8 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 for (int vk = 0; vk < VK; ++vk)
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
-                        vr[vk][i] = lds_u4(vt + swz<ROWS>(16 * vk + 2 * t + (i & 1) + 8 * (i >> 1), 16 * g));
-                read_scales(vsc, sc + ROWS * 4);
+                        vr[vk][i] = lds_u4(vt + swz<TROWS>(srow(16 * vk + 2 * t + (i & 1) + 8 * (i >> 1)), 16 * g));
+                read_scales(vsc, sc + TROWS * 4);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty_bar[stage]);
                 if constexpr (CH == 2) {
@@ -1244,9 +1268,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             }
 
             // this warp's groups of the run: CTA-local indices gidx + j with (gidx + j) % NC == warp
-            for (int j = ((warp - gidx) % NC + NC) % NC; j < r.len; j += NC) {
+            for (int j = ((ow - gidx) % NP + NP) % NP; j < r.len; j += NP) {
                 if (*cons_abort) continue;
-                const int stage = warp * SPW + my_slot;
+                const int stage = ow * SPW + my_slot;
                 bool ok = true;
                 if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -1438,40 +1462,45 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             break;
         }
 
-        const long long out_row = (static_cast<long long>(r.s) * Hkv + r.h) * G * D;
+        const long long out_row = (static_cast<long long>(r.s) * Hkv + r.h) * UG * D;
         // element o of the (s, h) state [G][D] in out (folded queries: [S, qfold, Hq, D])
         auto out_at = [&](int o) -> long long {
             return a.qfold > 1 ? qo_row(r.s, r.h, o / D, Hkv, G, a.qfold, a.seq_div) * D + (o % D) : out_row + o;
         };
-        const int slot_floats = 2 * G + G * D;
+        const int slot_floats = 2 * UG + UG * D;
         float *part = nullptr;
         if (r.pieces > 1)
             part = a.partials +
                    (static_cast<long long>(r.s * Hkv + r.h) * kMaxSplits + r.piece) * slot_floats;
-        for (int o = tid; o < G * D; o += CONS) {
-            const int hh = o / D;
+        for (int o = tid; o < UG * D; o += CONS) {
+            const int ro = o / D;          // row of the unit
+            const int hs = ro / G;         // PAIR: the head of the pair it belongs to
+            const int gr = ro - hs * G;    // its row among that head's warp states
+            const int oo = gr * D + (o - ro * D);
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < NC; ++w) M = fmaxf(M, sm_comb[w * G * (D + 2) + hh]);
+            for (int w = 0; w < NC; ++w)
+                if (w % HP == hs) M = fmaxf(M, sm_comb[w * G * (D + 2) + gr]);
             float Ls = 0.f, As = 0.f;
             if (M != -INFINITY) {
 #pragma unroll
                 for (int w = 0; w < NC; ++w) {
+                    if (w % HP != hs) continue;
                     const float *cw = sm_comb + w * G * (D + 2);
-                    const float mw = cw[hh];
+                    const float mw = cw[gr];
                     const float f = (mw == -INFINITY) ? 0.f : fast_exp2(mw - M);
-                    Ls += cw[G + hh] * f;
-                    As += cw[2 * G + o] * f;
+                    Ls += cw[G + gr] * f;
+                    As += cw[2 * G + oo] * f;
                 }
             }
             if (r.pieces == 1) {
                 const float v = Ls > 0.f ? As * (1.0f / (Ls + a.norm_eps)) : 0.f;
                 store_out(a.out, out_at(o), v, a.q_bf16);
             } else {
-                part[2 * G + o] = As;
+                part[2 * UG + o] = As;
                 if ((o % D) == 0) {
-                    part[hh] = M;
-                    part[G + hh] = Ls;
+                    part[ro] = M;
+                    part[UG + ro] = Ls;
                 }
             }
         }
@@ -1487,18 +1516,18 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 __threadfence();
                 const float *base =
                     a.partials + static_cast<long long>(r.s * Hkv + r.h) * kMaxSplits * slot_floats;
-                for (int o = tid; o < G * D; o += CONS) {
-                    const int hh = o / D;
+                for (int o = tid; o < UG * D; o += CONS) {
+                    const int ro = o / D;
                     float M = -INFINITY;
-                    for (int c = 0; c < r.pieces; ++c) M = fmaxf(M, __ldcg(base + c * slot_floats + hh));
+                    for (int c = 0; c < r.pieces; ++c) M = fmaxf(M, __ldcg(base + c * slot_floats + ro));
                     float Ls = 0.f, As = 0.f;
                     if (M != -INFINITY) {
                         for (int c = 0; c < r.pieces; ++c) {
                             const float *pc = base + c * slot_floats;
-                            const float mc = __ldcg(pc + hh);
+                            const float mc = __ldcg(pc + ro);
                             const float f = (mc == -INFINITY) ? 0.f : fast_exp2(mc - M);
-                            Ls += __ldcg(pc + G + hh) * f;
-                            As += __ldcg(pc + 2 * G + o) * f;
+                            Ls += __ldcg(pc + UG + ro) * f;
+                            As += __ldcg(pc + 2 * UG + o) * f;
                         }
                     }
                     const float v = Ls > 0.f ? As * (1.0f / (Ls + a.norm_eps)) : 0.f;

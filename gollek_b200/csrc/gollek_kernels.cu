@@ -561,6 +561,77 @@ int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     return GOLLEK_OK;
 }
 
+// int8 KV over 16-token pages in kv-head pairs (decode_tma_kernel<..., PAIR>): one 4 KB TMA
+// box per page holds both heads of a pair, so the copy path moves twice the bytes per box.
+// Needs bf16 q, an even number of kv heads, decode (no folded queries), and per-token scales
+// whose two heads are adjacent (head stride == block size) or per-page scales.
+// GOLLEK_I8_PAIR=0 (read per call) keeps the one-head-per-stage kernel.
+constexpr int kPairWarps = 10;
+
+template <int G>
+const void *pair_kernel() {
+    return reinterpret_cast<const void *>(&decode_tma_kernel<int8_t, 128, G, kPairWarps, false, 32, true>);
+}
+
+const void *pick_pair(int G) {
+    switch (G) {
+        case 1: return pair_kernel<1>();
+        case 2: return pair_kernel<2>();
+        case 4: return pair_kernel<4>();
+        case 8: return pair_kernel<8>();
+        default: return nullptr;
+    }
+}
+
+int try_pair(const V2 &p, int dev, int G, long long page_stride) {
+    const char *e = std::getenv("GOLLEK_I8_PAIR");
+    if (e && std::strcmp(e, "0") == 0) return kNotTaken;
+    if (p.kv_dtype != GOLLEK_DTYPE_I8 || p.D != 128 || p.BS != 16 || p.q_dtype != GOLLEK_DTYPE_BF16)
+        return kNotTaken;
+    if (p.qfold > 1 || p.Hkv % 2 != 0 || group_rows(p) != 32) return kNotTaken;
+    if (!tma_layout_ok(p, page_stride)) return kNotTaken;
+    const bool per_token = p.sts == 1 && p.shs == p.BS && (p.sps * 4) % 16 == 0 && (p.shs * 4) % 16 == 0 &&
+                           aligned16(p.ks) && aligned16(p.vs);
+    if (!per_token && p.sts != 0) return kNotTaken;
+    const void *fn = pick_pair(G);
+    if (!fn) return kNotTaken;
+    constexpr int kTrows = 64;  // 2 pages x 2 heads x 16 rows per K (or V) tile
+    const uint32_t tile = kTrows * 128;
+    const int max_ctas = sm_count(dev) * 2;
+    const int np = kPairWarps / 2;
+    DecodeSmem L0 = decode_smem_layout(1, true, p.D, G, kPairWarps, 0, p.S, max_ctas, kTrows);
+    int spw = static_cast<int>((kSmemBudget > L0.total ? kSmemBudget - L0.total : 0) / (2 * tile * np));
+    spw = std::min(spw, kMaxStagesPerWarp);
+    if (spw < 1) return kNotTaken;
+    const int stages = spw * np;
+    DecodeSmem L = decode_smem_layout(1, true, p.D, G, kPairWarps, stages, p.S, max_ctas, kTrows);
+    if (L.total > 227 * 1024 || L.q % 16 || L.p % 16 || L.scales % 16 || L.rstart % 8 || L.bars % 8)
+        return kNotTaken;
+    void *ws = nullptr;
+    size_t ws_cap = 0;
+    int rc = v2_workspace(p, dev, &ws, &ws_cap);
+    if (rc) return rc;
+    const long long rows_per_page = page_stride / p.D;
+    const long long rows =
+        p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page : (1LL << 31) - 1;
+    CUtensorMap tmk, tmv;
+    rc = encode_map(&tmk, p.k, p.kv_dtype, p.D, rows, 2 * p.BS);
+    if (!rc) rc = encode_map(&tmv, p.v, p.kv_dtype, p.D, rows, 2 * p.BS);
+    if (rc) return rc;
+    DecodeArgs a = v2_args(p, ws, ws_cap, page_stride, stages, 32);
+    a.num_kv_heads = p.Hkv / 2;  // units are kv-head pairs
+    a.box3d = 0;
+    a.scale_mode = per_token ? 0 : 1;
+    GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
+            "cudaFuncSetAttribute");
+    const int grid = sm_count(dev);
+    void *args[] = {&tmk, &tmv, &a};
+    GK_CUDA(cudaLaunchKernel(fn, dim3(grid), dim3((kPairWarps + 1) * 32), args, L.total,
+                             static_cast<cudaStream_t>(p.stream)),
+            "decode_tma_kernel (kv-head pairs) launch");
+    return GOLLEK_OK;
+}
+
 int run_v2(const V2 &p) {
     int dev = 0;
     GK_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
@@ -574,6 +645,10 @@ int run_v2(const V2 &p) {
 
     {
         const int rc = try_tc(p, dev, G, page_stride);
+        if (rc != kNotTaken) return rc;
+    }
+    {
+        const int rc = try_pair(p, dev, G, page_stride);
         if (rc != kNotTaken) return rc;
     }
     const void *fn = fast_eligible(p, G, page_stride);

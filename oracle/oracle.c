@@ -446,6 +446,8 @@ int oracle_update_cache(const float *key, const float *value, int T, const int *
     for (int t = 0; t < T; t++) {
         int seq = token_seq ? token_seq[t] : t;
         int pos = token_pos[t];
+        /* a position past the table has no block (the reference's lookup fails there too) */
+        if (pos < 0 || pos / BS >= maxB) return -1;
         int blockIdx = bt[(long long)seq * maxB + pos / BS];
         if (blockIdx < 0) return -1;
         int tokIdx = pos % BS;

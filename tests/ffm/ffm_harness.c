@@ -157,13 +157,13 @@ int main(int argc, char **argv) {
     DEV(cudaDeviceSynchronize());
     DEV(cudaMemcpy(out_v2, dout, sizeof out_v2, cudaMemcpyDeviceToHost));
 
-    /* append one token per sequence at position ctx (into the pages the tables name),
-     * then migrate three pages to free pages of the same pool */
+    /* append (overwrite) each sequence's last token, at position ctx - 1 of the pages the
+     * tables name, then migrate three pages to free pages of the same pool */
     static float key[S * H * D], val[S * H * D];
     static int32_t pos[S];
     for (int i = 0; i < S * H * D; ++i) key[i] = frand();
     for (int i = 0; i < S * H * D; ++i) val[i] = frand();
-    for (int s = 0; s < S; ++s) pos[s] = ctx[s];
+    for (int s = 0; s < S; ++s) pos[s] = ctx[s] - 1;
     void *dkey, *dval, *dpos, *dsrc, *ddst;
     int32_t src[3] = {bt[0], bt[MAXB + 1], bt[3 * MAXB + 2]}, dst[3] = {250, 251, 252};
     DEV(cudaMalloc(&dkey, sizeof key));

@@ -77,9 +77,9 @@ def test_ffm_calls_on_device_match_oracle(tmp_path, cuda_device):
     want2 = O.a2_compute(q, k, v, bt, ctx, 0.125, num_kv_heads=H, block_size=BS)[:, 0]
     assert np.abs(arr["out_v2"].reshape(S, H, D) - want2).max() <= 1e-4 * scale_ref
 
-    # append one token per sequence at position ctx, then migrate three pages
+    # each sequence's last token rewritten (position ctx - 1), then three pages migrated
     kf, vf = k.reshape(-1).copy(), v.reshape(-1).copy()
-    rc = O.update_cache(arr["key"].reshape(S, H, D), arr["val"].reshape(S, H, D), ctx.copy(), bt,
+    rc = O.update_cache(arr["key"].reshape(S, H, D), arr["val"].reshape(S, H, D), ctx - 1, bt,
                         storage=O.FP32, k_slab=kf, v_slab=vf, block_size=BS)
     assert rc == 0
     src = np.array([bt[0, 0], bt[1, 1], bt[3, 2]], np.int32)
