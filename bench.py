@@ -73,17 +73,21 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def traffic_per_launch(workload):
-    """ncu dram bytes per launch of the dominant kernel, from the committed summary."""
+def traffic_per_launch(workload, algorithmic=None):
+    """ncu dram bytes (read + write) per launch of the dominant kernel, from the committed
+    summary: its per-launch figure, or its traffic-to-algorithmic ratio times this launch's
+    algorithmic bytes (for a workload captured on a smaller case)."""
     p = os.path.join(ROOT, "profiles", f"ncu_{workload}.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.startswith("traffic_bytes_per_launch:"):
-            try:
+        try:
+            if line.startswith("traffic_bytes_per_launch:"):
                 return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
+            if line.startswith("traffic_ratio_to_algorithmic:") and algorithmic:
+                return float(line.split(":", 1)[1].split()[0]) * float(algorithmic)
+        except ValueError:
+            return None
     return None
 
 
@@ -559,7 +563,7 @@ def bench_decode(args, world, rank, local, workload=None, steps=None, cpu=True):
     achieved_min = -max_over_ranks(-achieved, world)
     alg_total = sum_over_ranks(float(alg), world)
     peak, peak_kind = peaks()
-    traffic = traffic_per_launch(workload)
+    traffic = traffic_per_launch(workload, alg)
 
     cpu_line = None
     if cpu and rank == 0 and world == 1 and not args.no_cpu_baseline:
