@@ -326,6 +326,10 @@ def cpu_decode_baseline(batch, seconds, threads=None, q=None, tq=1, max_seqs=Non
     bs = batch.sh["bs"]
     B = len(ctx_all)
     n_cap = B if max_seqs is None else max_seqs
+    # host memory: at most ~3 GB of gathered fp32 K and V pages in the sample
+    page_f32 = batch.hkv * bs * batch.sh["d"] * 4 * 2
+    cum = np.cumsum((ctx_all + bs - 1) // bs) * page_f32
+    n_cap = max(1, min(n_cap, int(np.searchsorted(cum, 3e9, side="right"))))
     scale = 1.0 / math.sqrt(batch.sh["d"])
 
     def sample(n):
