@@ -131,6 +131,21 @@ __device__ __forceinline__ void i8x4_to_f16x2_biased(uint32_t w, uint32_t &lo, u
 // 2^e as a float, exact, for e in [-126, 127].
 __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
 
+// Scores may exceed the running max used as the exponent reference by this much (log2
+// units) before the reference moves.
+constexpr float kLazyMax = 8.f;
+
+// Warp-wide bounded wait for an mbarrier phase; gives up when `abort` is set.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned limit,
+                                          volatile int *abort) {
+    for (unsigned i = 0; i < limit; ++i) {
+        if (*abort) return false;
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    }
+    raise_status(GOLLEK_STATUS_TIMEOUT);
+    return false;
+}
+
 // Unbiased exponent of a positive finite float (x in [2^e, 2^(e+1))); normals only.
 __device__ __forceinline__ int exp_of(float x) { return static_cast<int>((__float_as_uint(x) >> 23) & 0xffu) - 127; }
 
@@ -650,11 +665,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             const int lm_col = 8 * ((lane >> 3) & 1);
 
             for (int j = ((ow - gidx) % NP + NP) % NP; j < r.len; j += NP) {
-                if (*cons_abort) continue;
                 const int stage = ow * SPW + my_slot;
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
+                // every lane tests the phase (and the abort flag, read alongside); if it is
+                // not complete the warp spins together (bounded), giving up early once
+                // another warp has given up
+                bool ok = mbar_try_wait(&full_bar[stage], my_phase) & !*cons_abort;
+                if (!__all_sync(0xffffffffu, ok)) ok = warp_wait(&full_bar[stage], my_phase, wait_limit, cons_abort);
                 if (++my_slot == SPW) {
                     my_slot = 0;
                     my_phase ^= 1;
@@ -733,12 +749,28 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         p[nt][e] = x2;
                         mloc = fmaxf(mloc, x2);
                     }
-                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
-                const float mn = fmaxf(m_run, mloc);
-                const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
-                const float mref = (mn == -INFINITY) ? 0.f : mn;
-                m_run = mn;
+                // lazy running max (kLazyMax): the reference moves, and o and l are
+                // rescaled, only when a score passes it by more than 2^kLazyMax
+                if (__any_sync(0xffffffffu, mloc > m_run + kLazyMax)) {
+                    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+                    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+                    const float mn = fmaxf(m_run, mloc);
+                    const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
+                    m_run = mn;
+                    l_run *= alpha;
+                    if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                        const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * t);      // head 2t
+                        const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * t + 4);  // head 2t+1
+#pragma unroll
+                        for (int mt = 0; mt < KS; ++mt) {
+                            o[mt][0] *= al0;
+                            o[mt][1] *= al1;
+                            o[mt][2] *= al0;
+                            o[mt][3] *= al1;
+                        }
+                    }
+                }
+                const float mref = (m_run == -INFINITY) ? 0.f : m_run;
                 float psum = 0.f;
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt)
@@ -747,20 +779,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                         p[nt][e] = fast_exp2(p[nt][e] - mref);
                         psum += p[nt][e];
                     }
-                l_run = l_run * alpha + psum;
+                l_run += psum;
                 const uint32_t pb0 = pack2<KV>(p[0][0], p[0][1]);
                 const uint32_t pb1 = pack2<KV>(p[1][0], p[1][1]);
-                if (__any_sync(0xffffffffu, alpha != 1.f)) {
-                    const float al0 = __shfl_sync(0xffffffffu, alpha, 8 * t);      // head 2t
-                    const float al1 = __shfl_sync(0xffffffffu, alpha, 8 * t + 4);  // head 2t+1
-#pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        o[mt][0] *= al0;
-                        o[mt][1] *= al1;
-                        o[mt][2] *= al0;
-                        o[mt][3] *= al1;
-                    }
-                }
                 // ---------------- values
 #pragma unroll
                 for (int mt = 0; mt < KS; ++mt)
@@ -782,12 +803,26 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                             p2[nt][e] = x2;
                             mloc2 = fmaxf(mloc2, x2);
                         }
-                    mloc2 = fmaxf(mloc2, __shfl_xor_sync(0xffffffffu, mloc2, 1));
-                    mloc2 = fmaxf(mloc2, __shfl_xor_sync(0xffffffffu, mloc2, 2));
-                    const float mn2 = fmaxf(m_run2, mloc2);
-                    const float alpha2 = (mn2 == m_run2) ? 1.f : fast_exp2(m_run2 - mn2);
-                    const float mref2 = (mn2 == -INFINITY) ? 0.f : mn2;
-                    m_run2 = mn2;
+                    if (__any_sync(0xffffffffu, mloc2 > m_run2 + kLazyMax)) {
+                        mloc2 = fmaxf(mloc2, __shfl_xor_sync(0xffffffffu, mloc2, 1));
+                        mloc2 = fmaxf(mloc2, __shfl_xor_sync(0xffffffffu, mloc2, 2));
+                        const float mn2 = fmaxf(m_run2, mloc2);
+                        const float alpha2 = (mn2 == m_run2) ? 1.f : fast_exp2(m_run2 - mn2);
+                        m_run2 = mn2;
+                        l_run2 *= alpha2;
+                        if (__any_sync(0xffffffffu, alpha2 != 1.f)) {
+                            const float al0 = __shfl_sync(0xffffffffu, alpha2, 8 * t);      // head 8 + 2t
+                            const float al1 = __shfl_sync(0xffffffffu, alpha2, 8 * t + 4);  // head 9 + 2t
+#pragma unroll
+                            for (int mt = 0; mt < KS; ++mt) {
+                                o2[mt][0] *= al0;
+                                o2[mt][1] *= al1;
+                                o2[mt][2] *= al0;
+                                o2[mt][3] *= al1;
+                            }
+                        }
+                    }
+                    const float mref2 = (m_run2 == -INFINITY) ? 0.f : m_run2;
                     float psum2 = 0.f;
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt)
@@ -796,20 +831,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                             p2[nt][e] = fast_exp2(p2[nt][e] - mref2);
                             psum2 += p2[nt][e];
                         }
-                    l_run2 = l_run2 * alpha2 + psum2;
+                    l_run2 += psum2;
                     const uint32_t pc0 = pack2<KV>(p2[0][0], p2[0][1]);
                     const uint32_t pc1 = pack2<KV>(p2[1][0], p2[1][1]);
-                    if (__any_sync(0xffffffffu, alpha2 != 1.f)) {
-                        const float al0 = __shfl_sync(0xffffffffu, alpha2, 8 * t);      // head 8 + 2t
-                        const float al1 = __shfl_sync(0xffffffffu, alpha2, 8 * t + 4);  // head 9 + 2t
-#pragma unroll
-                        for (int mt = 0; mt < KS; ++mt) {
-                            o2[mt][0] *= al0;
-                            o2[mt][1] *= al1;
-                            o2[mt][2] *= al0;
-                            o2[mt][3] *= al1;
-                        }
-                    }
 #pragma unroll
                     for (int mt = 0; mt < KS; ++mt)
                         mma_16816<KV>(o2[mt], vb[mt][0], vb[mt][1], vb[mt][2], vb[mt][3], pc0, pc1);
@@ -995,11 +1019,12 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
             for (int mt = 0; mt < KS; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
             for (int j = ((ow - gidx) % NP + NP) % NP; j < r.len; j += NP) {
-                if (*cons_abort) continue;
                 const int stage = ow * SPW + my_slot;
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
+                // every lane tests the phase (and the abort flag, read alongside); if it is
+                // not complete the warp spins together (bounded), giving up early once
+                // another warp has given up
+                bool ok = mbar_try_wait(&full_bar[stage], my_phase) & !*cons_abort;
+                if (!__all_sync(0xffffffffu, ok)) ok = warp_wait(&full_bar[stage], my_phase, wait_limit, cons_abort);
                 if (++my_slot == SPW) {
                     my_slot = 0;
                     my_phase ^= 1;
@@ -1095,10 +1120,6 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 #pragma unroll
                         for (int e = 0; e < 2; ++e) s[0][nc][e] += s[1][nc][e];
                 }
-#pragma unroll
-                for (int nc = 0; nc < NTC; ++nc)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) s[0][nc][e] -= qbias;
                 // ---------------- online softmax for head g over tokens 8nt + 2t + e
                 // (vmax spans the group's window, the same for every row, so the V-scale
                 // exponent stays warp-uniform; row g's own causal bound masks its scores)
@@ -1107,77 +1128,106 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
                 bool valid[NTC][2];
                 float mloc = -INFINITY;
                 float vmax = 0.f;
+                bool vout = false;  // an in-window V scale outside [2^(ev-2), 2^(ev+3))
+                const float vband_lo = pow2i(max(-126, ev - 2)), vband_hi = pow2i(min(127, ev + 3));
 #pragma unroll
                 for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
                         const int tk = 8 * (nc * SETS + myset) + 2 * t + e;
-                        if (tk >= v_lo && tk < v_hi) vmax = fmaxf(vmax, vsc[nc][e]);
+                        if (tk >= v_lo && tk < v_hi) {
+                            vmax = fmaxf(vmax, vsc[nc][e]);
+                            vout |= !(vsc[nc][e] >= vband_lo && vsc[nc][e] < vband_hi);
+                        }
                         valid[nc][e] = row_used && tk >= v_lo && tk < row_hi;
-                        float x2 = s[0][nc][e] * qmul * ksc[nc][e];
-                        if (a.soft_cap > 0.f) x2 = a.soft_cap * tanhf(x2 / a.soft_cap) * a.post_scale;
-                        x2 = valid[nc][e] ? x2 : -INFINITY;
-                        p[nc][e] = x2;
-                        mloc = fmaxf(mloc, x2);
+                        p[nc][e] = (s[0][nc][e] - qbias) * (qmul * ksc[nc][e]);
                     }
-                // reduce over the quad's tokens and, with two sets, over the other set's
-                // row of the same head (lane + or - 4G): every (row, head) pair then agrees
-                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
-                mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
-                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-                vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-                if constexpr (SETS == 2) {
-                    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 4 * G));
-                    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4 * G));
+                if (a.soft_cap > 0.f) {
+#pragma unroll
+                    for (int nc = 0; nc < NTC; ++nc)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            p[nc][e] = a.soft_cap * tanhf(p[nc][e] / a.soft_cap) * a.post_scale;
                 }
-                const float mn = fmaxf(m_run, mloc);
-                const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
-                const float mref = (mn == -INFINITY) ? 0.f : mn;
-                m_run = mn;
-                // the V-scale exponent (warp-uniform: every quad sees the same tokens)
-                int ev_new = ev;
-                if (vmax > 0.f && vmax < INFINITY) {
-                    const int e0 = exp_of(vmax);
-                    if (!ev_set || e0 < ev - 2 || e0 > ev + 2) ev_new = max(-100, min(100, e0));
-                }
-                const float vmul = pow2i(-ev_new);
-                float psum = 0.f;
-                float pv[NTC][2];
 #pragma unroll
                 for (int nc = 0; nc < NTC; ++nc)
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
-                        const float pe = fast_exp2(p[nc][e] - mref);
-                        psum += pe;
-                        pv[nc][e] = valid[nc][e] ? pe * (vsc[nc][e] * vmul) : 0.f;
+                        p[nc][e] = valid[nc][e] ? p[nc][e] : -INFINITY;
+                        mloc = fmaxf(mloc, p[nc][e]);
                     }
-                l_run = l_run * alpha + psum;
-                // probabilities as the value MMA's B fragments: n-tile nt holds tokens
-                // 8nt + 2t, 8nt + 2t + 1 of head g, i.e. k rows 2t, 2t+1 (+8) of k-step nt / 2
-                // (two sets: this lane holds n-tile 2nc + myset; the odd one comes from the
-                // lane 4G above)
+                // probabilities relative to mref, V scales relative to 2^ev, as the value
+                // MMA's B fragments: n-tile nt holds tokens 8nt + 2t, 8nt + 2t + 1 of head g,
+                // i.e. k rows 2t, 2t+1 (+8) of k-step nt / 2 (two sets: this lane holds
+                // n-tile 2nc + myset; the odd one comes from the lane 4G above)
                 uint32_t pb[NTC];
-                float pmass = 0.f;
+                auto probs = [&](float mref, float vmul, float &psum, float &pmass) {
+                    psum = 0.f;
+                    pmass = 0.f;
 #pragma unroll
-                for (int nc = 0; nc < NTC; ++nc) {
-                    pb[nc] = pack2<__half>(pv[nc][0], pv[nc][1]);
-                    const float2 pr = unpack2<__half>(pb[nc]);
-                    pmass += pr.x + pr.y;
-                }
-                const float fac = ev_set ? alpha * pow2i(max(-126, min(127, ev - ev_new))) : alpha;
-                ps_run = ps_run * fac + pmass;
-                ev = ev_new;
-                ev_set = true;
-                if (__any_sync(0xffffffffu, fac != 1.f)) {
-                    const float al0 = __shfl_sync(0xffffffffu, fac, 8 * t);      // head 2t
-                    const float al1 = __shfl_sync(0xffffffffu, fac, 8 * t + 4);  // head 2t+1
+                    for (int nc = 0; nc < NTC; ++nc) {
+                        float pv[2];
 #pragma unroll
-                    for (int mt = 0; mt < KS; ++mt) {
-                        o[mt][0] *= al0;
-                        o[mt][1] *= al1;
-                        o[mt][2] *= al0;
-                        o[mt][3] *= al1;
+                        for (int e = 0; e < 2; ++e) {
+                            const float pe = fast_exp2(p[nc][e] - mref);
+                            psum += pe;
+                            pv[e] = valid[nc][e] ? pe * (vsc[nc][e] * vmul) : 0.f;
+                        }
+                        pb[nc] = pack2<__half>(pv[0], pv[1]);
+                        const float2 pr = unpack2<__half>(pb[nc]);
+                        pmass += pr.x + pr.y;
                     }
+                };
+                // Lazy running max: a group whose scores stay within 2^kLazyMax of the row's
+                // running max and whose V scales stay inside the exponent band keeps both
+                // references (probabilities up to 2^kLazyMax * 8 stay far inside f16; the
+                // final normalisation is relative to the same reference, so the result is
+                // unchanged), and needs no cross-lane reduction and no rescale.
+                const bool slow = mloc > m_run + kLazyMax || vout || !ev_set;
+                if (__any_sync(0xffffffffu, slow)) {
+                    // reduce over the quad's tokens and, with two sets, over the other set's
+                    // row of the same head (lane + or - 4G): every (row, head) pair then agrees
+                    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 1));
+                    mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 2));
+                    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
+                    vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
+                    if constexpr (SETS == 2) {
+                        mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, 4 * G));
+                        vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4 * G));
+                    }
+                    const float mn = fmaxf(m_run, mloc);
+                    const float alpha = (mn == m_run) ? 1.f : fast_exp2(m_run - mn);
+                    const float mref = (mn == -INFINITY) ? 0.f : mn;
+                    m_run = mn;
+                    // the V-scale exponent (warp-uniform: every quad sees the same tokens)
+                    int ev_new = ev;
+                    if (vmax > 0.f && vmax < INFINITY) {
+                        const int e0 = exp_of(vmax);
+                        if (!ev_set || e0 < ev - 2 || e0 > ev + 2) ev_new = max(-100, min(100, e0));
+                    }
+                    float psum, pmass;
+                    probs(mref, pow2i(-ev_new), psum, pmass);
+                    l_run = l_run * alpha + psum;
+                    const float fac = ev_set ? alpha * pow2i(max(-126, min(127, ev - ev_new))) : alpha;
+                    ps_run = ps_run * fac + pmass;
+                    ev = ev_new;
+                    ev_set = true;
+                    if (__any_sync(0xffffffffu, fac != 1.f)) {
+                        const float al0 = __shfl_sync(0xffffffffu, fac, 8 * t);      // head 2t
+                        const float al1 = __shfl_sync(0xffffffffu, fac, 8 * t + 4);  // head 2t+1
+#pragma unroll
+                        for (int mt = 0; mt < KS; ++mt) {
+                            o[mt][0] *= al0;
+                            o[mt][1] *= al1;
+                            o[mt][2] *= al0;
+                            o[mt][3] *= al1;
+                        }
+                    }
+                } else {
+                    float psum, pmass;
+                    probs(m_run == -INFINITY ? 0.f : m_run, pow2i(-ev), psum, pmass);
+                    l_run += psum;
+                    ps_run += pmass;
                 }
                 // ---------------- values: per k-step, rows 2t, 2t+1 (a0, a1) and 2t+8, 2t+9 (a2, a3)
 #pragma unroll
@@ -1269,11 +1319,9 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1)
 
             // this warp's groups of the run: CTA-local indices gidx + j with (gidx + j) % NC == warp
             for (int j = ((ow - gidx) % NP + NP) % NP; j < r.len; j += NP) {
-                if (*cons_abort) continue;
                 const int stage = ow * SPW + my_slot;
-                bool ok = true;
-                if (lane == 0) ok = mbar_wait(&full_bar[stage], my_phase, wait_limit);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
+                bool ok = mbar_try_wait(&full_bar[stage], my_phase) & !*cons_abort;
+                if (!__all_sync(0xffffffffu, ok)) ok = warp_wait(&full_bar[stage], my_phase, wait_limit, cons_abort);
                 if (++my_slot == SPW) {
                     my_slot = 0;
                     my_phase ^= 1;
