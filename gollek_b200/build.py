@@ -6,6 +6,7 @@
 from __future__ import annotations
 
 import argparse
+import fcntl
 import glob
 import os
 import shutil
@@ -41,15 +42,27 @@ def stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Builds the library if its sources are newer (or `force`).  Safe to call from several
+    processes at once (the ranks of one job): one builds under an exclusive file lock while
+    the others wait, then find it fresh; the new file replaces the old one atomically."""
     if not force and not stale():
         return LIB_PATH
     os.makedirs(LIB_DIR, exist_ok=True)
+    with open(os.path.join(LIB_DIR, ".build.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and not stale():
+            return LIB_PATH
+        return _build_locked(verbose)
+
+
+def _build_locked(verbose: bool) -> str:
+    tmp = f"{LIB_PATH}.{os.getpid()}.tmp"
     cmd = [
         nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-shared",
         "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
         "--expt-relaxed-constexpr",
         "-I", os.path.join(ROOT, "include"),
-        "-o", LIB_PATH + ".tmp", os.path.join(CSRC, "gollek_kernels.cu"),
+        "-o", tmp, os.path.join(CSRC, "gollek_kernels.cu"),
     ]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
@@ -64,7 +77,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError("nvcc failed building libgollek_kernels.so")
     if verbose:
         sys.stderr.write(r.stderr)
-    os.replace(LIB_PATH + ".tmp", LIB_PATH)
+    os.replace(tmp, LIB_PATH)
     return LIB_PATH
 
 
