@@ -12,6 +12,7 @@ import os
 import shutil
 import subprocess
 import sys
+import time
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -57,6 +58,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 def _build_locked(verbose: bool) -> str:
     tmp = f"{LIB_PATH}.{os.getpid()}.tmp"
+    # The output carries the build's start time, so a source edited while nvcc runs still
+    # reads as newer than the library.
+    start = time.time()
     cmd = [
         nvcc_path(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-shared",
         "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
@@ -77,6 +81,7 @@ def _build_locked(verbose: bool) -> str:
         raise RuntimeError("nvcc failed building libgollek_kernels.so")
     if verbose:
         sys.stderr.write(r.stderr)
+    os.utime(tmp, (start, start))
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

@@ -46,3 +46,28 @@ def test_one_compile_for_concurrent_callers(tmp_path):
     sizes = [q.get(timeout=10) for _ in procs]
     assert sizes == [8 * 4096] * 4
     assert open(tmp_path / "compiles").read() == "x"
+
+
+def test_source_edited_during_a_build_reads_stale(tmp_path, monkeypatch):
+    """A library whose build started before a source edit is stale, even though the edit
+    happened before the build finished."""
+    from gollek_b200 import build as B
+    src = tmp_path / "k.cu"
+    src.write_text("a")
+    lib = tmp_path / "lib.so"
+    monkeypatch.setattr(B, "LIB_PATH", str(lib))
+    monkeypatch.setattr(B, "sources", lambda: [str(src)])
+    real_run = B.subprocess.run
+
+    def fake_run(cmd, **kw):
+        out = cmd[cmd.index("-o") + 1]
+        time.sleep(0.05)
+        now = time.time()
+        os.utime(src, (now, now))  # edited mid-build ...
+        time.sleep(0.05)
+        open(out, "wb").write(b"\0")  # ... before the output is written
+        return real_run(["true"], **kw)
+
+    monkeypatch.setattr(B.subprocess, "run", fake_run)
+    B._build_locked(False)
+    assert B.stale()
