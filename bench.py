@@ -1010,17 +1010,22 @@ def bench_prefill(args, world, rank, local):
     d2h = hout.numel() * hout.element_size()
 
     # queries sharing one pass over the pages (the library's rule for causal calls with
-    # head_dim 128 and no window: F * G <= 16 rows for bf16 KV, <= 8 for int8 KV;
-    # GOLLEK_PREFILL_FOLD=0 turns it off)
+    # head_dim 128 and no window: F * G <= 16 rows for bf16 KV, or exactly 64 with bf16 q
+    # on the tensor-memory kernel (GOLLEK_PREFILL_TC=0: not), <= 8 for int8 KV;
+    # GOLLEK_PREFILL_FOLD=0 turns folding off)
     G = Hq // batch.hkv
     fold = 1
+    tc_rows = not int8 and os.environ.get("GOLLEK_PREFILL_TC", "1") != "0"
     if os.environ.get("GOLLEK_PREFILL_FOLD", "1") != "0":
-        f = (8 if int8 else 16) // G
+        f = 64
         while f > 1:
-            if Tq % f == 0:
+            if Tq % f == 0 and (f * G <= (8 if int8 else 16) or (tc_rows and f * G == 64)):
                 fold = f
                 break
             f >>= 1
+    kernel = ("prefill_tc_kernel (tcgen05; the folded rows are the MMA columns)" if fold * G == 64
+              else "decode_tma_kernel (queries folded into the MMA rows)" if fold > 1
+              else "decode_tma_kernel (per-query decode sequences)")
     kv_once = batch.algorithmic_bytes() - 2 * batch.q.numel() * batch.q_elem
     alg = kv_once + 2 * q.numel() * q.element_size()
     achieved = alg / ((t_ms / 1e3) / args.steps) / 1e9
@@ -1054,8 +1059,7 @@ def bench_prefill(args, world, rank, local):
                          "algorithmic_bytes_per_launch": alg,
                          "note": "numerator counts each page once per step (page-once ideal); "
                                  f"the kernel reads a page once per {fold} queries",
-                         "kernel": "decode_tma_kernel (queries folded into the MMA rows)"
-                                   if fold > 1 else "decode_tma_kernel (per-query decode sequences)"},
+                         "kernel": kernel},
             "e2e": {"value": B * Tq * world * _E2E.steps / (e_max / 1e3), "unit": "query tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": _E2E.steps,
                     "path": "pinned q, tables, lengths -> H2D -> gollek_paged_attention_prefill "

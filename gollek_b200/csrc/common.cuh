@@ -82,6 +82,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     return false;
 }
 
+// Bounded wait of one thread that also gives up (returning false, raising nothing) once
+// `abort` is set by a thread that gave up first.
+// sleep_ns > 0: sleep that long between tests (a polling thread then leaves the SM's
+// shared-memory pipe to the warps that do the work).
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                                   unsigned limit = kWaitLimit, unsigned sleep_ns = 0) {
+    for (unsigned i = 0; i < limit; ++i) {
+        if (*abort) return false;
+        if (mbar_try_wait(bar, parity)) return true;
+        if (sleep_ns) __nanosleep(sleep_ns);
+    }
+    raise_status(GOLLEK_STATUS_TIMEOUT);
+    return false;
+}
+
+// The same for a whole warp (every lane calls it; the result is warp-uniform).
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned limit,
+                                          volatile int *abort, unsigned sleep_ns = 0) {
+    for (unsigned i = 0; i < limit; ++i) {
+        if (__any_sync(0xffffffffu, *abort != 0)) return false;
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+        if (sleep_ns) __nanosleep(sleep_ns);
+    }
+    raise_status(GOLLEK_STATUS_TIMEOUT);
+    return false;
+}
+
 // Non-blocking test of an mbarrier phase.
 __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     uint32_t ok;

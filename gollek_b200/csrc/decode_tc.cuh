@@ -3,18 +3,12 @@
 // head_dim 128.
 //
 // Work: the same 16-token groups and stream-K CTA ranges as decode_tma_kernel
-// (decode_common.cuh).  A run of one (sequence, kv-head) is cut into tiles of up to
-// 8 groups = 128 tokens.  K and V tiles (32 KB each) live in two separate rings, so a
-// K tile is free again as soon as the score MMAs have read it, while a V tile waits
-// for the probabilities.
-//
-// Shared-memory tile layout: one group (16 tokens x 128 head-dim bf16 = 4 KB) is
-// [row half][64-column slab][8 rows][128 bytes], written by one 4-D TMA box in the
-// 128-byte swizzle, so every 8-token core group of a tile sits 2 KB after the previous
-// one and the two column slabs of a core group are 1 KB apart.  That is the canonical
-// 128B-swizzled operand layout: K-major for K (score MMA A operand, 2 KB between core
-// groups) and MN-major for V (value MMA A operand: slabs 1 KB apart along head_dim,
-// core groups 2 KB apart along tokens).
+// (decode_common.cuh), cut into tiles of up to 128 tokens (tc_tiles.cuh, which also
+// gives the tiles' shared-memory layout).  K and V tiles (32 KB each) live in two
+// separate rings, so a K tile is free again as soon as the score MMAs have read it,
+// while a V tile waits for the probabilities.  K is the score MMA's K-major A operand
+// (2 KB between 8-token core groups), V the value MMA's MN-major A operand (slabs 1 KB
+// apart along head_dim, core groups 2 KB apart along tokens).
 //
 // One CTA per SM, 8 warps:
 //   warp 0  K producer, warp 7 V producer: per tile, lane i looks up group i's page
@@ -39,16 +33,11 @@
 // CTA drains in-flight copies and MMAs before releasing tensor memory.
 #pragma once
 
-#include "decode_common.cuh"
-#include "tcgen05.cuh"
+#include "tc_tiles.cuh"
 
 namespace gk {
 
-constexpr int kTcGroups = 8;                            // 16-token groups per tile
-constexpr int kTcTokens = kTcGroups * kRows;            // 128
 constexpr int kTcN = 16;                                // MMA N: q heads, zero-padded
-constexpr uint32_t kTcGroupBytes = kRows * 256;         // 4 KB: K or V of one group
-constexpr uint32_t kTcTile = kTcGroups * kTcGroupBytes; // 32 KB: K or V of one tile
 constexpr uint32_t kTcOpBuf = kTcN * 256;               // 4 KB: 16 rows x 128 16-bit values
 constexpr int kTcThreads = 256;
 constexpr uint32_t kTcCols = 64;                        // S x2, O x2 (16 columns each)
@@ -93,13 +82,6 @@ __device__ __forceinline__ uint32_t sw128_off(int rows, int r, int c) {
     const int b = (c & 63) * 2;
     return static_cast<uint32_t>((c >> 6) * rows * 128 + r * 128 + ((((b >> 4) ^ (r & 7))) << 4) +
                                  (b & 15));
-}
-
-// Byte offset of 16-byte chunk `ch` (head_dim 8*ch .. 8*ch+7) of token `tok` in a K or V
-// tile (group layout above).
-__device__ __forceinline__ uint32_t tile_chunk_off(int tok, int ch) {
-    const int r8 = tok & 7;
-    return static_cast<uint32_t>((tok >> 3) * 2048 + (ch >> 3) * 1024 + r8 * 128 + (((ch & 7) ^ r8) << 4));
 }
 
 // SPLIT: fp32 q enters the score MMAs as bf16 hi + lo halves.
@@ -183,145 +165,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const Schedule sch = schedule_prologue(a, sm_prefix, sm_cprefix, sm_len, sm_rstart, &sm_misc[1],
                                            reinterpret_cast<int *>(sm_red));
 
-    // Tiles of this CTA in order: runs of the range, each cut into <= 8-group tiles.
-    struct TileIt {
-        long long x;  // first unit of the current run
-        Run r;
-        int tg0;      // first group of the tile within the run
-        int ri;       // run index within this CTA
-        int ti;       // tile index within this CTA
-        bool live;
-    };
-    auto it_begin = [&]() {
-        TileIt t;
-        t.x = sch.x_beg;
-        t.tg0 = 0;
-        t.ri = 0;
-        t.ti = 0;
-        t.live = t.x < sch.x_end;
-        if (t.live) {
-            t.r = sch.run_at(t.x);
-            sch.pieces(t.r);
-        }
-        return t;
-    };
-    auto it_next = [&](TileIt &t) {
-        ++t.ti;
-        t.tg0 += kTcGroups;
-        if (t.tg0 >= t.r.len) {
-            t.x += t.r.len;
-            ++t.ri;
-            t.tg0 = 0;
-            t.live = t.x < sch.x_end;
-            if (t.live) {
-                t.r = sch.run_at(t.x);
-                sch.pieces(t.r);
-            }
-        }
-    };
-    auto win_start_of = [&](int len) { return (a.window > 0 && len > a.window) ? len - a.window : 0; };
-
     if (warp == 0 || warp == 7) {
         // ========================================================= producers (K: warp 0, V: warp 7)
-        // Page ids are looked up two tiles ahead (block-table loads in flight while the
-        // current tile waits for its slot), so the loads' latency stays off the ring.
         const bool is_k = warp == 0;
-        const CUtensorMap *map = is_k ? &tm_k : &tm_v;
-        uint8_t *ring = is_k ? sm_kring : sm_vring;
-        uint64_t *full = is_k ? k_full : v_full;
-        uint64_t *empty = is_k ? k_empty : v_empty;
-        const int NR = is_k ? NK : NV;
-        const int R = a.block_size < kRows ? a.block_size : kRows;  // rows per TMA box
-        const int npg = kRows / R;                                  // pages per group (<= 2)
-        struct Loc {
-            int pid0, pid1, row_off;
-            unsigned loaded;
-        };
-        auto locate = [&](const TileIt &t) {
-            Loc l{0, 0, 0, 0u};
-            if (!t.live) return l;
-            const int ng = min(kTcGroups, t.r.len - t.tg0);
-            if (lane < ng) {
-                const int len = sm_len[t.r.s];
-                const int ws = win_start_of(len);
-                const int t0 = (ws / kRows + t.r.g + t.tg0 + lane) * kRows;
-                const int p_first = t0 / a.block_size;
-                l.row_off = a.block_size < kRows ? 0 : t0 % a.block_size;
-                const int pages_in_seq = (len + a.block_size - 1) / a.block_size;
-                const int *bt = a.block_tables + static_cast<long long>(t.r.s / a.seq_div) * a.max_blocks;
-                for (int j = 0; j < npg; ++j) {
-                    const int pg = p_first + j;
-                    if (pg < pages_in_seq && (pg + 1) * a.block_size > ws) {
-                        const int e = __ldg(bt + pg);
-                        if (j)
-                            l.pid1 = e;
-                        else
-                            l.pid0 = e;
-                        l.loaded |= 1u << j;
-                    }
-                }
-            }
-            return l;
-        };
-        int issued = 0;
-        TileIt ia = it_begin();
-        Loc la = locate(ia);
-        TileIt ib = ia;
-        if (ib.live) it_next(ib);
-        Loc lb = locate(ib);
-        while (ia.live) {
-            if (sm_misc[3]) break;
-            TileIt ic = ib;
-            if (ic.live) it_next(ic);
-            const Loc lc = locate(ic);
-            const int slot = ia.ti % NR;
-            const int rnd = ia.ti / NR;
-            uint32_t bytes = static_cast<uint32_t>(__popc(la.loaded)) * R * 256u;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
-            bool ok = true;
-            if (rnd > 0) {
-                if (lane == 0) ok = mbar_wait(&empty[slot], (rnd - 1) & 1);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-            }
-            if (!ok) {
-                if (lane == 0) sm_misc[3] = 1;
-                break;
-            }
-            if (lane == 0) mbar_arrive_expect_tx(&full[slot], bytes);
-            __syncwarp();
-            if (la.loaded) {
-                uint8_t *dst = ring + static_cast<uint32_t>(slot) * kTcTile + lane * kTcGroupBytes;
-#pragma unroll 1
-                for (int j = 0; j < npg; ++j) {
-                    if (!((la.loaded >> j) & 1)) continue;
-                    int e = j ? la.pid1 : la.pid0;
-                    if (e < 0 || (a.num_blocks > 0 && e >= a.num_blocks)) {
-                        raise_status(GOLLEK_STATUS_BAD_BLOCK_ID);
-                        e = 0;
-                    }
-                    const long long y = static_cast<long long>(e) * a.page_rows +
-                                        static_cast<long long>(ia.r.h) * a.block_size + la.row_off;
-                    tma_load_4d(dst + j * R * 256, map, 0, 0, 0, static_cast<int>(y >> 3), &full[slot]);
-                }
-            }
-            ++issued;
-            ia = ib;
-            la = lb;
-            ib = ic;
-            lb = lc;
-        }
-        // every copy issued lands before the CTA's shared memory is released
-        if (lane == 0)
-            for (int k = max(0, issued - NR); k < issued; ++k) mbar_wait(&full[k % NR], (k / NR) & 1);
-        __syncwarp();
+        tc_producer(a, sch, sm_len, &sm_misc[3], is_k ? &tm_k : &tm_v, is_k ? sm_kring : sm_vring,
+                    is_k ? k_full : v_full, is_k ? k_empty : v_empty, is_k ? NK : NV, lane);
     } else if (warp == 1) {
         // ========================================================= score MMAs
         if (lane == 0) {
             constexpr uint32_t id_s = umma_idesc_16bit(kTcTokens, kTcN, 1, 0, 0);
             const uint32_t k_base = smem_u32(sm_kring);
             const uint32_t q_base = smem_u32(sm_q);
-            for (TileIt is = it_begin(); is.live; it_next(is)) {
+            for (TileIt is = tile_begin(sch); is.live; tile_next(sch, is)) {
                 const int slot = is.ti % NK;
                 const int sb = is.ti & 1;
                 bool ok = mbar_wait(&k_full[slot], (is.ti / NK) & 1);
@@ -360,7 +215,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             constexpr uint32_t id_o = umma_idesc_16bit(D, kTcN, 1, 1, 0);
             const uint32_t v_base = smem_u32(sm_vring);
             const uint32_t p_base = smem_u32(sm_p);
-            for (TileIt ip = it_begin(); ip.live; it_next(ip)) {
+            for (TileIt ip = tile_begin(sch); ip.live; tile_next(sch, ip)) {
                 const int slot = ip.ti % NV;
                 const int sb = ip.ti & 1;
                 bool ok = mbar_wait(&p_full[sb], (ip.ti >> 1) & 1);
@@ -473,7 +328,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
 
         int prev_ti = -1;
-        for (TileIt it = it_begin(); it.live;) {
+        for (TileIt it = tile_begin(sch); it.live;) {
             const int ti = it.ti;
             const int sb = ti & 1;
             const Run r = it.r;
@@ -492,7 +347,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[sb]);
             const int len = sm_len[r.s];
-            const int ws = win_start_of(len);
+            const int ws = tc_win_start(a, len);
             const int gi = row >> 4;
             const int tok = (ws / kRows + r.g + it.tg0 + gi) * kRows + (row & 15);
             const bool valid = gi < ng && tok >= ws && tok < len;
@@ -552,7 +407,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int h = 0; h < G; ++h) alpha_prev[h] = alpha[h];
             prev_ti = ti;
-            it_next(it);
+            tile_next(sch, it);
             if (!run_end) continue;
 
             // ---------------- end of the run

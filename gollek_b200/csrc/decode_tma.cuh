@@ -135,17 +135,6 @@ __device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) 
 // units) before the reference moves.
 constexpr float kLazyMax = 8.f;
 
-// Warp-wide bounded wait for an mbarrier phase; gives up when `abort` is set.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned limit,
-                                          volatile int *abort) {
-    for (unsigned i = 0; i < limit; ++i) {
-        if (*abort) return false;
-        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-    }
-    raise_status(GOLLEK_STATUS_TIMEOUT);
-    return false;
-}
-
 // Unbiased exponent of a positive finite float (x in [2^e, 2^(e+1))); normals only.
 __device__ __forceinline__ int exp_of(float x) { return static_cast<int>((__float_as_uint(x) >> 23) & 0xffu) - 127; }
 

@@ -21,6 +21,7 @@
 #include "decode_tma.cuh"
 #include "kv_append.cuh"
 #include "kv_migrate.cuh"
+#include "prefill_tc.cuh"
 
 namespace gk {
 namespace {
@@ -561,6 +562,60 @@ int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     return GOLLEK_OK;
 }
 
+// Folded multi-query calls of 64 rows per (chunk, kv-head) unit -- F queries x G heads --
+// with bf16 KV and bf16 q, head_dim 128: the tensor-memory kernel whose MMA columns are
+// the folded rows (prefill_tc.cuh), so one pass over the pages serves 64 rows.  (At 32
+// rows two passes of the 16-row mma.sync kernel measured faster, so 32-row folds are not
+// formed.)  GOLLEK_PREFILL_TC=0 (read per call) leaves these calls to the 16-row kernel.
+bool prefill_tc_enabled() {
+    const char *e = std::getenv("GOLLEK_PREFILL_TC");
+    return !(e && e[0] == '0');
+}
+
+int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
+    if (p.qfold <= 1 || !prefill_tc_enabled()) return kNotTaken;
+    if (p.kv_dtype != GOLLEK_DTYPE_BF16 || p.q_dtype != GOLLEK_DTYPE_BF16 || p.D != 128 || p.window > 0)
+        return kNotTaken;
+    if (G != 64) return kNotTaken;
+    const void *fn = reinterpret_cast<const void *>(&prefill_tc_kernel<64>);
+    if (!tma_layout_ok(p, page_stride) || !aligned16(p.q) || !aligned16(p.out)) return kNotTaken;
+    const long long rows_per_page = page_stride / p.D;
+    if (rows_per_page % 8 != 0) return kNotTaken;
+    const int ctas = sm_count(dev);
+    static const int kRings[][2] = {{2, 3}, {2, 2}, {1, 2}};
+    int nk = 0, nv = 0;
+    PtSmem L{};
+    for (const auto &rg : kRings) {
+        L = pt_smem_layout(rg[0], rg[1], p.S, ctas);
+        if (L.total <= 227 * 1024) {
+            nk = rg[0];
+            nv = rg[1];
+            break;
+        }
+    }
+    if (!nk) return kNotTaken;
+    void *ws = nullptr;
+    size_t ws_cap = 0;
+    int rc = v2_workspace(p, dev, &ws, &ws_cap);
+    if (rc) return rc;
+    const long long rows =
+        p.num_blocks > 0 ? static_cast<long long>(p.num_blocks) * rows_per_page : (1LL << 31) - 8;
+    const int box_rows = p.BS < kRows ? p.BS : kRows;
+    CUtensorMap tmk, tmv;
+    rc = encode_map4(&tmk, p.k, rows, box_rows);
+    if (!rc) rc = encode_map4(&tmv, p.v, rows, box_rows);
+    if (rc) return rc;
+    DecodeArgs a = v2_args(p, ws, ws_cap, page_stride, nk);
+    a.num_vstages = nv;
+    GK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, L.total),
+            "cudaFuncSetAttribute");
+    void *args[] = {&tmk, &tmv, &a};
+    GK_CUDA(cudaLaunchKernel(fn, dim3(ctas), dim3(kPtThreads), args, L.total,
+                             static_cast<cudaStream_t>(p.stream)),
+            "prefill_tc_kernel launch");
+    return GOLLEK_OK;
+}
+
 // int8 KV over 16-token pages in kv-head pairs (decode_tma_kernel<..., PAIR>): one 4 KB TMA
 // box per page holds both heads of a pair, so the copy path moves twice the bytes per box.
 // Needs bf16 q, an even number of kv heads, decode (no folded queries), and per-token scales
@@ -643,6 +698,10 @@ int run_v2(const V2 &p) {
     cudaStream_t st = static_cast<cudaStream_t>(p.stream);
     if (p.S == 0) return GOLLEK_OK;
 
+    {
+        const int rc = try_prefill_tc(p, dev, G, page_stride);
+        if (rc != kNotTaken) return rc;
+    }
     {
         const int rc = try_tc(p, dev, G, page_stride);
         if (rc != kNotTaken) return rc;
@@ -1065,14 +1124,17 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
                           (kv_dtype == GOLLEK_DTYPE_BF16 || kv_dtype == GOLLEK_DTYPE_F16 ||
                            kv_dtype == GOLLEK_DTYPE_F32 ||
                            (kv_dtype == GOLLEK_DTYPE_I8 && head_dim == 128));
-    // rows of the kernel: 16 for bf16 KV with head_dim 128, else 8
-    const int max_rows = (kv_dtype == GOLLEK_DTYPE_BF16 && head_dim == 128) ? 16 : 8;
+    // rows of the kernels: 16 for bf16 KV with head_dim 128 (the mma.sync kernel), else 8;
+    // with bf16 q also exactly 64 (the tensor-memory kernel)
+    const bool bf16_128 = kv_dtype == GOLLEK_DTYPE_BF16 && head_dim == 128;
+    const int max_rows = bf16_128 ? 16 : 8;
+    const bool tc_rows = bf16_128 && q_dtype == GOLLEK_DTYPE_BF16 && prefill_tc_enabled();
     auto next_fold = [&](int below) {
         for (int f = below >> 1; f > 1; f >>= 1)
-            if (num_queries % f == 0 && G * f <= max_rows) return f;
+            if (num_queries % f == 0 && (G * f <= max_rows || (tc_rows && G * f == 64))) return f;
         return 1;
     };
-    int F = foldable ? next_fold(2 * max_rows) : 1;
+    int F = foldable ? next_fold(2 * 64) : 1;
     for (;;) {
         const int C = num_queries / F;
         const long long nv = static_cast<long long>(num_seqs) * C;

@@ -236,3 +236,51 @@ def test_prefill_page_once_fp32(cuda_device, monkeypatch, hq, hkv, d, tq):
         assert np.abs(got - want).max() <= tol
     assert not folded[0][0, :max(0, tq - 4)].any()
     assert ops.device_status(cuda_device.index or 0) == 0
+
+
+def _nan_past_context(k, v, bt, ctx, bs=16):
+    """NaN in every pool row no query may read: past each context in its last page."""
+    k, v = k.copy(), v.copy()
+    for s, n in enumerate(ctx):
+        if n > 0 and n % bs:
+            page = bt[s, (n - 1) // bs]
+            k[page, :, n % bs:] = np.nan
+            v[page, :, n % bs:] = np.nan
+    return k, v
+
+
+@pytest.mark.parametrize("hq,hkv,tq,soft_cap", [(32, 8, 16, 0.0), (64, 8, 8, 0.0), (64, 8, 16, 0.0),
+                                                (16, 8, 32, 0.0), (8, 8, 64, 0.0), (32, 8, 48, 0.0),
+                                                (32, 8, 16, 30.0), (32, 8, 8, 0.0)])
+def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap):
+    """Folded calls of 64 rows (F queries x G heads) per (chunk, kv-head): the
+    tensor-memory kernel (prefill_tc.cuh), against the oracle and against the same call on
+    the 16-row mma.sync fold (GOLLEK_PREFILL_TC=0); Tq = 8 with G = 4 (32 rows) stays on the
+    16-row fold.  Lengths below Tq give rows that see
+    nothing or part of a tile; NaN fills the page rows past every context; the 6000-token
+    sequence splits across CTAs (merged by the last piece); Tq = 48 gives three 16-query
+    chunks per sequence."""
+    from gollek_b200 import ops
+    q, k, v, bt, ctx = _case([2, 5, 17, 300, 2100, 6000], tq, hq, hkv, seed=130 + tq + hq)
+    qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
+    scale = 1 / math.sqrt(128)
+    want = _oracle(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=16, causal=1, soft_cap=soft_cap)
+    kn, vn = _nan_past_context(kb, vb, bt, ctx)
+
+    def run():
+        return ops.paged_attention_prefill(_t(qb, cuda_device, torch.bfloat16),
+                                           _t(kn, cuda_device, torch.bfloat16),
+                                           _t(vn, cuda_device, torch.bfloat16), _t(bt, cuda_device),
+                                           _t(ctx, cuda_device), num_kv_heads=hkv, block_size=16,
+                                           scale=scale, causal=True, num_blocks=k.shape[0],
+                                           soft_cap=soft_cap).float().cpu().numpy()
+
+    tc = [run() for _ in range(2)]
+    monkeypatch.setenv("GOLLEK_PREFILL_TC", "0")
+    mma = run()
+    for got in tc + [mma]:
+        assert np.isfinite(got).all()
+        np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    np.testing.assert_allclose(tc[0], mma, atol=1e-2, rtol=0)
+    assert not tc[0][0, :max(0, tq - 2)].any()
+    assert ops.device_status(cuda_device.index or 0) == 0
