@@ -586,7 +586,7 @@ int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
     int nk = 0, nv = 0;
     PtSmem L{};
     for (const auto &rg : kRings) {
-        L = pt_smem_layout(rg[0], rg[1], p.S, ctas);
+        L = pt_smem_layout(G, rg[0], rg[1], p.S, ctas);
         if (L.total <= 227 * 1024) {
             nk = rg[0];
             nv = rg[1];
