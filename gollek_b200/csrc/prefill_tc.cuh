@@ -46,7 +46,7 @@ constexpr uint32_t kPtCols = 512;  // S x2 (128 columns each), O (128)
 
 // Polling waits sleep this long between tests, which keeps the shared-memory pipe free for
 // the MMA issue, tensor-memory loads and stores of the working warps.
-constexpr unsigned kPtPollNs = 128;
+constexpr unsigned kPtPollNs = 256;
 
 // Scores may exceed their row's exponent reference by this much (log2 units) before the
 // reference moves: probabilities stay below 2^8, far inside bf16 and fp32.
