@@ -82,16 +82,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
     return false;
 }
 
+// mbarrier test that may suspend the thread until the phase completes, for at most ns
+// nanoseconds (the suspend-time hint of mbarrier.try_wait).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Tests allowed to a wait whose tests suspend for up to 20 us each (kSuspendNs): the same
+// bound in time as kWaitLimit plain tests, about a third of a second.
+constexpr uint32_t kSuspendNs = 20000;
+constexpr unsigned kSuspendTries = kWaitLimit >> 10;
+
 // Bounded wait of one thread that also gives up (returning false, raising nothing) once
 // `abort` is set by a thread that gave up first.
-// sleep_ns > 0: sleep that long between tests (a polling thread then leaves the SM's
-// shared-memory pipe to the warps that do the work).
+// suspend_ns > 0: each test may suspend the thread until the phase completes, for up to
+// that long (the waiting thread then leaves the SM's issue slots and shared-memory pipe to
+// the warps that do the work; give a limit of tries to match, e.g. kSuspendTries).
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                                   unsigned limit = kWaitLimit, unsigned sleep_ns = 0) {
+                                                   unsigned limit = kWaitLimit, uint32_t suspend_ns = 0) {
     for (unsigned i = 0; i < limit; ++i) {
         if (*abort) return false;
-        if (mbar_try_wait(bar, parity)) return true;
-        if (sleep_ns) __nanosleep(sleep_ns);
+        if (suspend_ns ? mbar_try_wait_suspend(bar, parity, suspend_ns) : mbar_try_wait(bar, parity)) return true;
     }
     raise_status(GOLLEK_STATUS_TIMEOUT);
     return false;
@@ -99,11 +118,12 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parit
 
 // The same for a whole warp (every lane calls it; the result is warp-uniform).
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, unsigned limit,
-                                          volatile int *abort, unsigned sleep_ns = 0) {
+                                          volatile int *abort, uint32_t suspend_ns = 0) {
     for (unsigned i = 0; i < limit; ++i) {
         if (__any_sync(0xffffffffu, *abort != 0)) return false;
-        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
-        if (sleep_ns) __nanosleep(sleep_ns);
+        if (__all_sync(0xffffffffu, suspend_ns ? mbar_try_wait_suspend(bar, parity, suspend_ns)
+                                               : mbar_try_wait(bar, parity)))
+            return true;
     }
     raise_status(GOLLEK_STATUS_TIMEOUT);
     return false;

@@ -72,13 +72,14 @@ __device__ __forceinline__ int tc_win_start(const DecodeArgs &a, int len) {
 
 // Producer warp of one ring (K or V): per tile, lane i looks up group i's page (two tiles
 // ahead, so the block-table loads are in flight while the current tile waits for its
-// slot) and, once the slot is free (polled every sleep_ns), issues the group's TMA box.
+// slot) and, once the slot is free, issues the group's TMA box (suspend_ns > 0: each test
+// of the slot may suspend the lane that long, see mbar_wait_or_abort).
 // Gives up (raising *abort) if a wait for a free slot runs out or another warp gave up;
 // every copy it issued has landed when it returns.
 __device__ inline void tc_producer(const DecodeArgs &a, const Schedule &sch, const int *sm_len,
                                    volatile int *abort, const CUtensorMap *map, uint8_t *ring,
                                    uint64_t *full, uint64_t *empty, int NR, int lane,
-                                   unsigned sleep_ns = 0) {
+                                   uint32_t suspend_ns = 0) {
     const int R = a.block_size < kRows ? a.block_size : kRows;  // rows per TMA box
     const int npg = kRows / R;                                  // pages per group (<= 2)
     struct Loc {
@@ -129,7 +130,9 @@ __device__ inline void tc_producer(const DecodeArgs &a, const Schedule &sch, con
         for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
         bool ok = true;
         if (rnd > 0) {
-            if (lane == 0) ok = mbar_wait_or_abort(&empty[slot], (rnd - 1) & 1, abort, kWaitLimit, sleep_ns);
+            if (lane == 0)
+                ok = mbar_wait_or_abort(&empty[slot], (rnd - 1) & 1, abort, suspend_ns ? kSuspendTries : kWaitLimit,
+                                        suspend_ns);
             ok = __shfl_sync(0xffffffffu, ok, 0);
         }
         if (!ok) {
