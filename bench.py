@@ -1010,7 +1010,7 @@ def bench_prefill(args, world, rank, local):
     d2h = hout.numel() * hout.element_size()
 
     # queries sharing one pass over the pages (the library's rule for causal calls with
-    # head_dim 128 and no window: F * G <= 16 rows for bf16 KV, or exactly 64 with bf16 q
+    # head_dim 128 and no window: F * G <= 16 rows for bf16 KV, or 32 / 64 with bf16 q
     # on the tensor-memory kernel (GOLLEK_PREFILL_TC=0: not), <= 8 for int8 KV;
     # GOLLEK_PREFILL_FOLD=0 turns folding off)
     G = Hq // batch.hkv
@@ -1019,11 +1019,11 @@ def bench_prefill(args, world, rank, local):
     if os.environ.get("GOLLEK_PREFILL_FOLD", "1") != "0":
         f = 64
         while f > 1:
-            if Tq % f == 0 and (f * G <= (8 if int8 else 16) or (tc_rows and f * G == 64)):
+            if Tq % f == 0 and (f * G <= (8 if int8 else 16) or (tc_rows and f * G in (32, 64))):
                 fold = f
                 break
             f >>= 1
-    kernel = ("prefill_tc_kernel (tcgen05; the folded rows are the MMA columns)" if fold * G == 64
+    kernel = ("prefill_tc_kernel (tcgen05; the folded rows are the MMA rows)" if fold * G in (32, 64)
               else "decode_tma_kernel (queries folded into the MMA rows)" if fold > 1
               else "decode_tma_kernel (per-query decode sequences)")
     kv_once = batch.algorithmic_bytes() - 2 * batch.q.numel() * batch.q_elem

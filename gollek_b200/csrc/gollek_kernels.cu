@@ -562,11 +562,10 @@ int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     return GOLLEK_OK;
 }
 
-// Folded multi-query calls of 64 rows per (chunk, kv-head) unit -- F queries x G heads --
-// with bf16 KV and bf16 q, head_dim 128: the tensor-memory kernel whose MMA columns are
-// the folded rows (prefill_tc.cuh), so one pass over the pages serves 64 rows.  (At 32
-// rows two passes of the 16-row mma.sync kernel measured faster, so 32-row folds are not
-// formed.)  GOLLEK_PREFILL_TC=0 (read per call) leaves these calls to the 16-row kernel.
+// Folded multi-query calls of 32 or 64 rows per (chunk, kv-head) unit -- F queries x G
+// heads -- with bf16 KV and bf16 q, head_dim 128: the tensor-memory kernel whose MMA rows
+// are the folded rows (prefill_tc.cuh), so one pass over the pages serves up to 64 rows.
+// GOLLEK_PREFILL_TC=0 (read per call) leaves these calls to the 16-row mma.sync kernel.
 bool prefill_tc_enabled() {
     const char *e = std::getenv("GOLLEK_PREFILL_TC");
     return !(e && e[0] == '0');
@@ -576,8 +575,9 @@ int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
     if (p.qfold <= 1 || !prefill_tc_enabled()) return kNotTaken;
     if (p.kv_dtype != GOLLEK_DTYPE_BF16 || p.q_dtype != GOLLEK_DTYPE_BF16 || p.D != 128 || p.window > 0)
         return kNotTaken;
-    if (G != 64) return kNotTaken;
-    const void *fn = reinterpret_cast<const void *>(&prefill_tc_kernel<64>);
+    if (G != 32 && G != 64) return kNotTaken;
+    const void *fn = G == 64 ? reinterpret_cast<const void *>(&prefill_tc_kernel<64>)
+                             : reinterpret_cast<const void *>(&prefill_tc_kernel<32>);
     if (!tma_layout_ok(p, page_stride) || !aligned16(p.q) || !aligned16(p.out)) return kNotTaken;
     const long long rows_per_page = page_stride / p.D;
     if (rows_per_page % 8 != 0) return kNotTaken;
@@ -1125,13 +1125,13 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
                            kv_dtype == GOLLEK_DTYPE_F32 ||
                            (kv_dtype == GOLLEK_DTYPE_I8 && head_dim == 128));
     // rows of the kernels: 16 for bf16 KV with head_dim 128 (the mma.sync kernel), else 8;
-    // with bf16 q also exactly 64 (the tensor-memory kernel)
+    // with bf16 q also 32 or 64 (the tensor-memory kernel)
     const bool bf16_128 = kv_dtype == GOLLEK_DTYPE_BF16 && head_dim == 128;
     const int max_rows = bf16_128 ? 16 : 8;
     const bool tc_rows = bf16_128 && q_dtype == GOLLEK_DTYPE_BF16 && prefill_tc_enabled();
     auto next_fold = [&](int below) {
         for (int f = below >> 1; f > 1; f >>= 1)
-            if (num_queries % f == 0 && (G * f <= max_rows || (tc_rows && G * f == 64))) return f;
+            if (num_queries % f == 0 && (G * f <= max_rows || (tc_rows && (G * f == 32 || G * f == 64)))) return f;
         return 1;
     };
     int F = foldable ? next_fold(2 * 64) : 1;

@@ -2,9 +2,8 @@
 // speculative tokens, over the paged cache) on the 5th-generation tensor cores, for bf16
 // KV and bf16 q with head_dim 128.
 //
-// The folded rows of a (chunk, kv-head) unit -- F queries x G heads, NQ = 64 of them
-// (qo_row, decode_common.cuh; 32 works too, but the library forms no 32-row folds) -- are
-// the M rows of both MMAs, so one thread owns one row: its exponent reference and
+// The folded rows of a (chunk, kv-head) unit -- F queries x G heads, NQ = 32 or 64 of them
+// (qo_row, decode_common.cuh) -- are the M rows of both MMAs, so one thread owns one row: its exponent reference and
 // normaliser stay in its registers, with no cross-thread reduction, and the values
 // accumulate in tensor memory over the whole run:
 //

@@ -160,7 +160,7 @@ GOLLEK_API size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_
  * Every other argument as gollek_paged_attention_v2.  Causal calls over bf16/f16/fp32 KV,
  * or int8 KV with head_dim 128, without a window read each page once per F queries: F (the
  * largest power of two that divides num_queries with F * num_q_heads / num_kv_heads <= 16
- * for bf16 KV with head_dim 128, <= 8 otherwise -- or == 64 for bf16 KV and bf16 q with
+ * for bf16 KV with head_dim 128, <= 8 otherwise -- or 32 or 64 for bf16 KV and bf16 q with
  * head_dim 128, on the tcgen05 kernel) queries of a sequence share one pass over its pages
  * as extra rows, each row with its own causal bound.  Other calls read each query's
  * context once per query.  The environment variables GOLLEK_PREFILL_FOLD=0 (read per call)

@@ -253,10 +253,9 @@ def _nan_past_context(k, v, bt, ctx, bs=16):
                                                 (16, 8, 32, 0.0), (8, 8, 64, 0.0), (32, 8, 48, 0.0),
                                                 (32, 8, 16, 30.0), (32, 8, 8, 0.0)])
 def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap):
-    """Folded calls of 64 rows (F queries x G heads) per (chunk, kv-head): the
+    """Folded calls of 32 or 64 rows (F queries x G heads) per (chunk, kv-head): the
     tensor-memory kernel (prefill_tc.cuh), against the oracle and against the same call on
-    the 16-row mma.sync fold (GOLLEK_PREFILL_TC=0); Tq = 8 with G = 4 (32 rows) stays on the
-    16-row fold.  Lengths below Tq give rows that see
+    the 16-row mma.sync fold (GOLLEK_PREFILL_TC=0).  Lengths below Tq give rows that see
     nothing or part of a tile; NaN fills the page rows past every context; the 6000-token
     sequence splits across CTAs (merged by the last piece); Tq = 48 gives three 16-query
     chunks per sequence."""
