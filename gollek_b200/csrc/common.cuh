@@ -96,10 +96,11 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t pa
     return ok != 0;
 }
 
-// Tests allowed to a wait whose tests suspend for up to 20 us each (kSuspendNs): the same
-// bound in time as kWaitLimit plain tests, about a third of a second.
+// Tests allowed to a wait whose tests suspend for up to 20 us each (kSuspendNs): at most
+// about 5 s if every test suspends the whole hint, and still well above any wait of a
+// working kernel if tests return early.
 constexpr uint32_t kSuspendNs = 20000;
-constexpr unsigned kSuspendTries = kWaitLimit >> 10;
+constexpr unsigned kSuspendTries = kWaitLimit >> 6;
 
 // Bounded wait of one thread that also gives up (returning false, raising nothing) once
 // `abort` is set by a thread that gave up first.

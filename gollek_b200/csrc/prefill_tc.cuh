@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         const uint32_t t_lane = static_cast<uint32_t>(32 * (warp - 4)) << 16;
         const int gm = NQ / a.qfold;                 // heads per query
         const int qshift = a.qfold - 1 - c / gm;     // row c's query sees the positions before len - qshift
-        const unsigned wl = a.wait_limit ? max(1u, a.wait_limit >> 10) : kSuspendTries;
+        const unsigned wl = a.wait_limit ? max(1u, a.wait_limit >> 6) : kSuspendTries;
         const int slot_floats = 2 * NQ + NQ * D;
         const float qs = a.q_scale;
         const bool cap = a.soft_cap > 0.f;
