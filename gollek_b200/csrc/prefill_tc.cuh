@@ -26,7 +26,7 @@
 //   warp 3 allocates tensor memory; lane 0 issues the score MMAs;
 //   warp 6 lane 0 issues the value MMAs (overwriting O at a run's first tile);
 //   warps 4 .. 4 + NQ/32 - 1 (tensor-memory lane quarters 0, 1): row threads, whose
-//     sub-partitions hold no polling warp;
+//     sub-partitions hold no producer or issuer;
 //   warps 0, 1 (and 5 when NQ = 32): zero the outputs of empty sequences, then idle.
 // The row warps never wait for one another: each arrives on the barriers the MMA issuers
 // wait for, and at a run's end each writes its own rows (a split run's last arriving warp
@@ -43,11 +43,11 @@ namespace gk {
 constexpr int kPtThreads = 256;
 constexpr uint32_t kPtCols = 512;  // S x2 (128 columns each), O (128)
 
-// Waits suspend the waiting thread until the phase completes (kSuspendNs per test), which
-// leaves the issue slots and the shared-memory pipe to the MMA issue, tensor-memory loads
-// and stores of the working warps (measured against polling with 256 / 512 ns sleeps:
-// 0.503 against 0.527 / 0.514 ms at Tq = 16).
-constexpr uint32_t kPtPollNs = kSuspendNs;
+// Waits suspend the waiting thread until the phase completes (up to this long per test),
+// which leaves the issue slots and the shared-memory pipe to the MMA issue, tensor-memory
+// loads and stores of the working warps (measured against polling with 256 / 512 ns
+// sleeps: 0.503 against 0.527 / 0.514 ms at Tq = 16).
+constexpr uint32_t kPtSuspendNs = kSuspendNs;
 
 // Scores may exceed their row's exponent reference by this much (log2 units) before the
 // reference moves: probabilities stay below 2^8, far inside bf16 and fp32.
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         // ========================================================= producers (K: warp 2, V: warp 7)
         const bool is_k = warp == 2;
         tc_producer(a, sch, sm_len, abort, is_k ? &tm_k : &tm_v, is_k ? sm_kring : sm_vring,
-                    is_k ? k_full : v_full, is_k ? k_empty : v_empty, is_k ? NK : NV, lane, kPtPollNs);
+                    is_k ? k_full : v_full, is_k ? k_empty : v_empty, is_k ? NK : NV, lane, kPtSuspendNs);
     } else if (warp == 3) {
         // ========================================================= score MMAs
         if (lane == 0) {
@@ -179,10 +179,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (TileIt is = tile_begin(sch); is.live; tile_next(sch, is)) {
                 const int slot = is.ti % NK;
                 const int sb = is.ti & 1;
-                bool ok = mbar_wait_or_abort(&k_full[slot], (is.ti / NK) & 1, abort, kSuspendTries, kPtPollNs);
+                bool ok = mbar_wait_or_abort(&k_full[slot], (is.ti / NK) & 1, abort, kSuspendTries, kPtSuspendNs);
                 if (ok && is.ti >= 2)
-                    ok = mbar_wait_or_abort(&s_free[sb], ((is.ti >> 1) + 1) & 1, abort, kSuspendTries, kPtPollNs);
-                if (ok && is.tg0 == 0) ok = mbar_wait_or_abort(q_full, is.ri & 1, abort, kSuspendTries, kPtPollNs);
+                    ok = mbar_wait_or_abort(&s_free[sb], ((is.ti >> 1) + 1) & 1, abort, kSuspendTries, kPtSuspendNs);
+                if (ok && is.tg0 == 0) ok = mbar_wait_or_abort(q_full, is.ri & 1, abort, kSuspendTries, kPtSuspendNs);
                 if (!ok) {
                     *abort = 1;
                     break;
@@ -209,10 +209,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (TileIt ip = tile_begin(sch); ip.live; tile_next(sch, ip)) {
                 const int slot = ip.ti % NV;
                 const int sb = ip.ti & 1;
-                bool ok = mbar_wait_or_abort(&p_full[sb], (ip.ti >> 1) & 1, abort, kSuspendTries, kPtPollNs);
-                if (ok) ok = mbar_wait_or_abort(&v_full[slot], (ip.ti / NV) & 1, abort, kSuspendTries, kPtPollNs);
+                bool ok = mbar_wait_or_abort(&p_full[sb], (ip.ti >> 1) & 1, abort, kSuspendTries, kPtSuspendNs);
+                if (ok) ok = mbar_wait_or_abort(&v_full[slot], (ip.ti / NV) & 1, abort, kSuspendTries, kPtSuspendNs);
                 if (ok && ip.tg0 == 0 && ip.ri > 0)
-                    ok = mbar_wait_or_abort(o_free, (ip.ri - 1) & 1, abort, kSuspendTries, kPtPollNs);
+                    ok = mbar_wait_or_abort(o_free, (ip.ri - 1) & 1, abort, kSuspendTries, kPtSuspendNs);
                 if (!ok) {
                     *abort = 1;
                     break;
@@ -357,9 +357,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             const int lo = max(ws - t0, 0);
             const int vhi = min(len - t0, ng * kRows);
             const int hi = min(vhi, len - qshift - t0);
-            bool ok = warp_wait(&s_full[sb], (ti >> 1) & 1, wl, abort, kPtPollNs);
+            bool ok = warp_wait(&s_full[sb], (ti >> 1) & 1, wl, abort, kPtSuspendNs);
             // the probability buffer is free once the value MMAs of tile ti - 2 completed
-            if (ok && ti >= 2) ok = warp_wait(&o_done[sb], ((ti - 2) >> 1) & 1, wl, abort, kPtPollNs);
+            if (ok && ti >= 2) ok = warp_wait(&o_done[sb], ((ti - 2) >> 1) & 1, wl, abort, kPtSuspendNs);
             if (!ok) {
                 bad = true;
                 break;
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 if (it.tg0 > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                     // O holds this run's earlier tiles: once the previous tile's value MMAs
                     // are complete, scale row c's O by alpha
-                    if (!warp_wait(&o_done[(ti - 1) & 1], ((ti - 1) >> 1) & 1, wl, abort, kPtPollNs)) {
+                    if (!warp_wait(&o_done[(ti - 1) & 1], ((ti - 1) >> 1) & 1, wl, abort, kPtSuspendNs)) {
                         bad = true;
                         break;
                     }
@@ -401,7 +401,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             if (lo > 0 || vhi < kTcTokens) {
                 // clear V rows [0, lo) and [vhi, 128) once the tile's V copies have landed
                 const int vslot = ti % NV;
-                if (!warp_wait(&v_full[vslot], (ti / NV) & 1, wl, abort, kPtPollNs)) {
+                if (!warp_wait(&v_full[vslot], (ti / NV) & 1, wl, abort, kPtSuspendNs)) {
                     bad = true;
                     break;
                 }
@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             if (!run_end) continue;
 
             // ---------------- end of the run: row c of O, normalised, out
-            if (!warp_wait(&o_done[sb], (ti >> 1) & 1, wl, abort, kPtPollNs)) {
+            if (!warp_wait(&o_done[sb], (ti >> 1) & 1, wl, abort, kPtSuspendNs)) {
                 bad = true;
                 break;
             }
