@@ -562,19 +562,21 @@ int try_tc(const V2 &p, int dev, int G, long long page_stride) {
     return GOLLEK_OK;
 }
 
-// Folded multi-query calls of 32 or 64 rows per (chunk, kv-head) unit -- F queries x G
-// heads -- with bf16 KV and bf16 q, head_dim 128: the tensor-memory kernel whose MMA rows
-// are the folded rows (prefill_tc.cuh), so one pass over the pages serves up to 64 rows.
-// GOLLEK_PREFILL_TC=0 (read per call) leaves these calls to the 16-row mma.sync kernel.
+// 32 or 64 rows per (sequence or chunk, kv-head) unit with bf16 KV and bf16 q, head_dim
+// 128 -- folded multi-query calls (F queries x G heads), and decode with G = 32 or 64 q
+// heads per kv head (multi-query-attention models) -- on the tensor-memory kernel whose MMA
+// rows are those rows (prefill_tc.cuh), so one pass over the pages serves up to 64 rows.
+// GOLLEK_PREFILL_TC=0 (read per call) leaves folded calls to the 16-row mma.sync kernel;
+// decode with such groups has no other kernel (GOLLEK_ERR_UNSUPPORTED without this one).
 bool prefill_tc_enabled() {
     const char *e = std::getenv("GOLLEK_PREFILL_TC");
     return !(e && e[0] == '0');
 }
 
 int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
-    if (p.qfold <= 1 || !prefill_tc_enabled()) return kNotTaken;
-    if (p.kv_dtype != GOLLEK_DTYPE_BF16 || p.q_dtype != GOLLEK_DTYPE_BF16 || p.D != 128 || p.window > 0)
-        return kNotTaken;
+    if (!prefill_tc_enabled()) return kNotTaken;
+    // (folded calls come without a window; decode may have one)
+    if (p.kv_dtype != GOLLEK_DTYPE_BF16 || p.q_dtype != GOLLEK_DTYPE_BF16 || p.D != 128) return kNotTaken;
     if (G != 32 && G != 64) return kNotTaken;
     const void *fn = G == 64 ? reinterpret_cast<const void *>(&prefill_tc_kernel<64>)
                              : reinterpret_cast<const void *>(&prefill_tc_kernel<32>);

@@ -1,9 +1,10 @@
 // prefill_tc.cuh -- multi-query paged attention (the queries of a prefill chunk, or
-// speculative tokens, over the paged cache) on the 5th-generation tensor cores, for bf16
-// KV and bf16 q with head_dim 128.
+// speculative tokens, over the paged cache), and decode with 32 or 64 q heads per kv head,
+// on the 5th-generation tensor cores, for bf16 KV and bf16 q with head_dim 128.
 //
-// The folded rows of a (chunk, kv-head) unit -- F queries x G heads, NQ = 32 or 64 of them
-// (qo_row, decode_common.cuh) -- are the M rows of both MMAs, so one thread owns one row: its exponent reference and
+// The rows of a (chunk or sequence, kv-head) unit -- F queries x G heads folded, or the G
+// heads of one query; NQ = 32 or 64 of them (qo_row, decode_common.cuh) -- are the M rows
+// of both MMAs, so one thread owns one row: its exponent reference and
 // normaliser stay in its registers, with no cross-thread reduction, and the values
 // accumulate in tensor memory over the whole run:
 //
