@@ -970,7 +970,7 @@ def bench_prefill(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     int8 = args.workload == "prefill_int8"
-    batch = DecodeBatch("decode_int8" if int8 else "decode_bf16", args.seed + rank, dev)
+    batch = DecodeBatch("decode_int8" if int8 else "decode_bf16", args.seed, dev, value_seed=args.seed + rank)
     B, Hq, D = batch.q.shape
     Tq = args.tq
     g = torch.Generator(device=dev).manual_seed(args.seed + 11 + rank)
