@@ -113,25 +113,27 @@ def test_window_and_softcap(cuda_device, window, soft_cap):
     _fp32_close(out.cpu().numpy(), want)
 
 
-@pytest.mark.parametrize("hq,hkv,window,soft_cap", [(32, 1, 0, 0.0), (64, 1, 0, 0.0), (256, 8, 0, 0.0),
-                                                    (64, 2, 100, 0.0), (32, 1, 0, 30.0), (64, 1, 40, 5.0)])
-def test_bf16_large_groups(cuda_device, monkeypatch, hq, hkv, window, soft_cap):
+@pytest.mark.parametrize("hq,hkv,window,soft_cap,bs", [(32, 1, 0, 0.0, 16), (64, 1, 0, 0.0, 16),
+                                                       (256, 8, 0, 0.0, 16), (64, 2, 100, 0.0, 16),
+                                                       (32, 1, 0, 30.0, 16), (64, 1, 40, 5.0, 16),
+                                                       (32, 1, 0, 0.0, 8), (64, 2, 0, 0.0, 64)])
+def test_bf16_large_groups(cuda_device, monkeypatch, hq, hkv, window, soft_cap, bs):
     """Decode with 32 or 64 q heads per kv head (multi-query-attention models): the
     tensor-memory kernel of prefill_tc.cuh with the heads as its rows, against the oracle,
-    twice (bit-identical); windows and soft-cap; an empty context gives zeros; the
-    9000-token context splits across CTAs.  No other kernel serves these groups: with
+    twice (bit-identical); windows and soft-cap; pages of 8, 16 and 64 tokens; an empty
+    context gives zeros; the 9000-token context splits across CTAs.  No other kernel serves these groups: with
     GOLLEK_PREFILL_TC=0 the call is refused as unsupported."""
     from gollek_b200 import ops
     ctx = [1, 31, 32, 33, 200, 517, 1024, 2049, 0, 77, 9000]
-    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=128, bs=16, seed=hq + hkv + window, kv_std=0.5)
+    q, k, v, bt, ctx = decode_case(ctx, hq=hq, hkv=hkv, d=128, bs=bs, seed=hq + hkv + window + bs, kv_std=0.5)
     qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
     scale = 1.0 / math.sqrt(128)
-    want = oracle_decode(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=16, window=window, soft_cap=soft_cap)
+    want = oracle_decode(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=bs, window=window, soft_cap=soft_cap)
 
     def run():
         out = ops.paged_attention(_t(qb, cuda_device, torch.bfloat16), _t(kb, cuda_device, torch.bfloat16),
                                   _t(vb, cuda_device, torch.bfloat16), _t(bt, cuda_device),
-                                  _t(ctx, cuda_device), num_kv_heads=hkv, block_size=16, scale=scale,
+                                  _t(ctx, cuda_device), num_kv_heads=hkv, block_size=bs, scale=scale,
                                   soft_cap=soft_cap, sliding_window=window, num_blocks=k.shape[0])
         return out.float().cpu().numpy()
 

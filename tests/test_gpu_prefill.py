@@ -249,10 +249,12 @@ def _nan_past_context(k, v, bt, ctx, bs=16):
     return k, v
 
 
-@pytest.mark.parametrize("hq,hkv,tq,soft_cap", [(32, 8, 16, 0.0), (64, 8, 8, 0.0), (64, 8, 16, 0.0),
-                                                (16, 8, 32, 0.0), (8, 8, 64, 0.0), (32, 8, 48, 0.0),
-                                                (32, 8, 16, 30.0), (32, 8, 8, 0.0)])
-def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap):
+@pytest.mark.parametrize("hq,hkv,tq,soft_cap,bs", [(32, 8, 16, 0.0, 16), (64, 8, 8, 0.0, 16),
+                                                   (64, 8, 16, 0.0, 16), (16, 8, 32, 0.0, 16),
+                                                   (8, 8, 64, 0.0, 16), (32, 8, 48, 0.0, 16),
+                                                   (32, 8, 16, 30.0, 16), (32, 8, 8, 0.0, 16),
+                                                   (32, 8, 16, 0.0, 8), (32, 8, 8, 0.0, 32)])
+def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap, bs):
     """Folded calls of 32 or 64 rows (F queries x G heads) per (chunk, kv-head): the
     tensor-memory kernel (prefill_tc.cuh), against the oracle and against the same call on
     the 16-row mma.sync fold (GOLLEK_PREFILL_TC=0).  Lengths below Tq give rows that see
@@ -260,17 +262,17 @@ def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap):
     sequence splits across CTAs (merged by the last piece); Tq = 48 gives three 16-query
     chunks per sequence."""
     from gollek_b200 import ops
-    q, k, v, bt, ctx = _case([2, 5, 17, 300, 2100, 6000], tq, hq, hkv, seed=130 + tq + hq)
+    q, k, v, bt, ctx = _case([2, 5, 17, 300, 2100, 6000], tq, hq, hkv, seed=130 + tq + hq + bs, bs=bs)
     qb, kb, vb = O.round_bf16(q), O.round_bf16(k), O.round_bf16(v)
     scale = 1 / math.sqrt(128)
-    want = _oracle(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=16, causal=1, soft_cap=soft_cap)
-    kn, vn = _nan_past_context(kb, vb, bt, ctx)
+    want = _oracle(qb, kb, vb, bt, ctx, scale, hkv=hkv, bs=bs, causal=1, soft_cap=soft_cap)
+    kn, vn = _nan_past_context(kb, vb, bt, ctx, bs=bs)
 
     def run():
         return ops.paged_attention_prefill(_t(qb, cuda_device, torch.bfloat16),
                                            _t(kn, cuda_device, torch.bfloat16),
                                            _t(vn, cuda_device, torch.bfloat16), _t(bt, cuda_device),
-                                           _t(ctx, cuda_device), num_kv_heads=hkv, block_size=16,
+                                           _t(ctx, cuda_device), num_kv_heads=hkv, block_size=bs,
                                            scale=scale, causal=True, num_blocks=k.shape[0],
                                            soft_cap=soft_cap).float().cpu().numpy()
 
