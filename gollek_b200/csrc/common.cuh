@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "gollek_kernels.h"
 
 namespace gk {
@@ -30,6 +32,26 @@ constexpr unsigned kPollLimit = 1u << 24;
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Two floats -> one 32-bit register of the 16-bit MMA type (x0 in the low half).
+template <typename KV>
+__device__ __forceinline__ uint32_t pack2(float x0, float x1) {
+    if constexpr (std::is_same<KV, __half>::value) {
+        __half2 h = __floats2half2_rn(x0, x1);
+        return *reinterpret_cast<uint32_t *>(&h);
+    } else {
+        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+}
+
+template <typename KV>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+    if constexpr (std::is_same<KV, __half>::value)
+        return __half22float2(*reinterpret_cast<__half2 *>(&w));
+    else
+        return make_float2(bf16_lo(w), bf16_hi(w));
+}
 
 // ----------------------------------------------------------------- mbarrier
 

@@ -81,26 +81,6 @@ __device__ __forceinline__ void decode_word<float>(uint32_t w, float *f) {
     f[0] = __uint_as_float(w);
 }
 
-// Two floats -> one 32-bit register of the 16-bit MMA type (x0 in the low half).
-template <typename KV>
-__device__ __forceinline__ uint32_t pack2(float x0, float x1) {
-    if constexpr (std::is_same<KV, __half>::value) {
-        __half2 h = __floats2half2_rn(x0, x1);
-        return *reinterpret_cast<uint32_t *>(&h);
-    } else {
-        __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-        return *reinterpret_cast<uint32_t *>(&h);
-    }
-}
-
-template <typename KV>
-__device__ __forceinline__ float2 unpack2(uint32_t w) {
-    if constexpr (std::is_same<KV, __half>::value)
-        return __half22float2(*reinterpret_cast<__half2 *>(&w));
-    else
-        return make_float2(bf16_lo(w), bf16_hi(w));
-}
-
 // c += A(16x16, row) * B(16x8, col) with fp32 accumulation.
 template <typename KV>
 __device__ __forceinline__ void mma_16816(float *c, uint32_t a0, uint32_t a1, uint32_t a2,
