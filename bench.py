@@ -29,6 +29,7 @@ Java; no JDK exists here), on all host threads.
 from __future__ import annotations
 
 import argparse
+import copy
 import json
 import math
 import os
@@ -1037,35 +1038,36 @@ def bench_prefill(args, world, rank, local):
         cpu = cpu_decode_baseline(batch, args.cpu_seconds, q=q, tq=Tq)
         cpu.pop("per_seq_s", None)
         cpu.pop("seconds_per_step", None)
-    if rank == 0:
-        sh = batch.sh
-        print(json.dumps({
-            "metric": METRIC, "value": value, "unit": "query tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8 KV, bf16 q/out, f32 accumulate" if int8 else "bf16 KV/q/out, f32 accumulate",
-            "data": "synthetic (seeded; config 3 shapes)" if int8 else "synthetic (seeded; config 2 shapes)",
-            "config": {"workload": f"multi_query_causal_tq{Tq}_{'config3' if int8 else 'config2'}_pool",
-                       "batch_per_gpu": B,
-                       "queries_per_seq": Tq, "queries_per_page_pass": fold, "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"],
-                       "head_dim": sh["d"], "block_size": sh["bs"],
-                       "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
-                       "parallelism": f"independent batches x{world}",
-                       "l2": f"no flush: {kv_once / 1e9:.2f} GB of KV per step per GPU > 126 MB L2"},
-            "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
-                         "frac": achieved_min / peak,
-                         "traffic": traffic_per_launch(f"prefill{'_int8' if int8 else ''}_tq{Tq}"),
-                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                         "algorithmic_bytes_per_launch": alg,
-                         "note": "numerator counts each page once per step (page-once ideal); "
-                                 f"the kernel reads a page once per {fold} queries",
-                         "kernel": kernel},
-            "e2e": {"value": B * Tq * world * _E2E.steps / (e_max / 1e3), "unit": "query tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": _E2E.steps,
-                    "path": "pinned q, tables, lengths -> H2D -> gollek_paged_attention_prefill "
-                            "-> D2H of out, serialised on one stream"},
-            "gpu_launches": 2 * args.steps, "clocks": clocks, "cpu_baseline": cpu,
-        }), flush=True)
+    if rank != 0:
+        return None
+    sh = batch.sh
+    return {
+        "metric": METRIC, "value": value, "unit": "query tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 KV, bf16 q/out, f32 accumulate" if int8 else "bf16 KV/q/out, f32 accumulate",
+        "data": "synthetic (seeded; config 3 shapes)" if int8 else "synthetic (seeded; config 2 shapes)",
+        "config": {"workload": f"multi_query_causal_tq{Tq}_{'config3' if int8 else 'config2'}_pool",
+                   "batch_per_gpu": B,
+                   "queries_per_seq": Tq, "queries_per_page_pass": fold, "num_q_heads": sh["hq"], "num_kv_heads": sh["hkv"],
+                   "head_dim": sh["d"], "block_size": sh["bs"],
+                   "context": f"{sh['dist']}[{sh['lo']},{sh['hi']}]",
+                   "parallelism": f"independent batches x{world}",
+                   "l2": f"no flush: {kv_once / 1e9:.2f} GB of KV per step per GPU > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": achieved_min, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_min / peak,
+                     "traffic": traffic_per_launch(f"prefill{'_int8' if int8 else ''}_tq{Tq}"),
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                     "algorithmic_bytes_per_launch": alg,
+                     "note": "numerator counts each page once per step (page-once ideal); "
+                             f"the kernel reads a page once per {fold} queries",
+                     "kernel": kernel},
+        "e2e": {"value": B * Tq * world * _E2E.steps / (e_max / 1e3), "unit": "query tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": _E2E.steps,
+                "path": "pinned q, tables, lengths -> H2D -> gollek_paged_attention_prefill "
+                        "-> D2H of out, serialised on one stream"},
+        "gpu_launches": 2 * args.steps, "clocks": clocks, "cpu_baseline": cpu,
+    }
 
 
 def bench_cow(args, world, rank, local):
@@ -1278,12 +1280,18 @@ SUB_DROP = ("metric", "n_gpus", "higher_is_better", "vs_baseline", "data")
 def bench_default(args, world, rank, local):
     """The default line: BASELINE config 2 as the headline, with the other BASELINE configs
     measured in the same run as sub-objects -- config 1 through the legacy symbol, config 3
-    (int8 KV), config 5 (KV heads sharded over the N GPUs, strong scaling) and, at N >= 2,
-    config 4 (prefill ranks push KV blocks to decode ranks over NVLink)."""
+    (int8 KV), config 5 (KV heads sharded over the N GPUs, strong scaling), multi-query
+    attention with 16 queries per sequence on config 2's pool and, at N >= 2, config 4
+    (prefill ranks push KV blocks to decode ranks over NVLink)."""
     head = bench_decode(args, world, rank, local, "decode_bf16")
     subs = {"config1": bench_config1(args, world, rank, local),
             "decode_int8": bench_decode(args, world, rank, local, "decode_int8"),
             "longctx": bench_decode(args, world, rank, local, "longctx")}
+    # multi-query attention (16 causal queries per sequence on config 2's pool): one pass
+    # over the pages on the tcgen05 kernel (64 folded rows per kv head)
+    pa = copy.copy(args)
+    pa.workload, pa.tq, pa.no_cpu_baseline = "prefill", 16, True
+    subs["prefill_tq16"] = bench_prefill(pa, world, rank, local)
     if world >= 2 and world % 2 == 0:
         subs["migrate"] = bench_migrate(args, world, rank, local, steps=min(args.steps, 20))
     else:
