@@ -123,7 +123,7 @@ GOLLEK_API int gollek_cuda_device_name(char *buf, int len);
  *   scale      softmax scale; soft_cap > 0 applies cap*tanh(score/cap).
  *   GQA group num_q_heads / num_kv_heads: up to 8 for every storage type; 16 for bf16 KV
  *              with head_dim 128; 32 and 64 (multi-query-attention models) for bf16 KV
- *              and bf16 q with head_dim 128, up to 6,880 sequences per call; otherwise
+ *              and bf16 q with head_dim 128, up to 6,879 sequences per call; otherwise
  *              GOLLEK_ERR_UNSUPPORTED.
  *   workspace  split-K scratch of at least gollek_paged_attention_workspace_size(...)
  *              bytes, zero-filled before its first use and left zeroed by every call
