@@ -167,6 +167,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     const Schedule sch = schedule_prologue(a, sm_prefix, sm_cprefix, sm_len, sm_rstart, &sm_misc[1],
                                            reinterpret_cast<int *>(smem + L.p));
 
+    // tries of a suspending wait (GOLLEK_TEST_WAIT_LIMIT shortens them, as for every wait)
+    const unsigned it_tries = a.wait_limit ? max(1u, a.wait_limit >> 6) : kSuspendTries;
+
     if (warp == 2 || warp == 7) {
         // ========================================================= producers (K: warp 2, V: warp 7)
         const bool is_k = warp == 2;
@@ -180,10 +183,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (TileIt is = tile_begin(sch); is.live; tile_next(sch, is)) {
                 const int slot = is.ti % NK;
                 const int sb = is.ti & 1;
-                bool ok = mbar_wait_or_abort(&k_full[slot], (is.ti / NK) & 1, abort, kSuspendTries, kPtSuspendNs);
+                bool ok = mbar_wait_or_abort(&k_full[slot], (is.ti / NK) & 1, abort, it_tries, kPtSuspendNs);
                 if (ok && is.ti >= 2)
-                    ok = mbar_wait_or_abort(&s_free[sb], ((is.ti >> 1) + 1) & 1, abort, kSuspendTries, kPtSuspendNs);
-                if (ok && is.tg0 == 0) ok = mbar_wait_or_abort(q_full, is.ri & 1, abort, kSuspendTries, kPtSuspendNs);
+                    ok = mbar_wait_or_abort(&s_free[sb], ((is.ti >> 1) + 1) & 1, abort, it_tries, kPtSuspendNs);
+                if (ok && is.tg0 == 0) ok = mbar_wait_or_abort(q_full, is.ri & 1, abort, it_tries, kPtSuspendNs);
                 if (!ok) {
                     *abort = 1;
                     break;
@@ -210,10 +213,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             for (TileIt ip = tile_begin(sch); ip.live; tile_next(sch, ip)) {
                 const int slot = ip.ti % NV;
                 const int sb = ip.ti & 1;
-                bool ok = mbar_wait_or_abort(&p_full[sb], (ip.ti >> 1) & 1, abort, kSuspendTries, kPtSuspendNs);
-                if (ok) ok = mbar_wait_or_abort(&v_full[slot], (ip.ti / NV) & 1, abort, kSuspendTries, kPtSuspendNs);
+                bool ok = mbar_wait_or_abort(&p_full[sb], (ip.ti >> 1) & 1, abort, it_tries, kPtSuspendNs);
+                if (ok) ok = mbar_wait_or_abort(&v_full[slot], (ip.ti / NV) & 1, abort, it_tries, kPtSuspendNs);
                 if (ok && ip.tg0 == 0 && ip.ri > 0)
-                    ok = mbar_wait_or_abort(o_free, (ip.ri - 1) & 1, abort, kSuspendTries, kPtSuspendNs);
+                    ok = mbar_wait_or_abort(o_free, (ip.ri - 1) & 1, abort, it_tries, kPtSuspendNs);
                 if (!ok) {
                     *abort = 1;
                     break;

@@ -120,6 +120,9 @@ __device__ inline void tc_producer(const DecodeArgs &a, const Schedule &sch, con
     Loc lb = locate(ib);
     while (ia.live) {
         if (*abort) break;
+        // test-only fault injection: CTA 0 stops issuing at this tile (the copies are
+        // simply never made, so a consumer's bounded wait gives up; nothing else changes)
+        if (a.fault_skip_group >= 0 && blockIdx.x == 0 && ia.ti == a.fault_skip_group) break;
         TileIt ic = ib;
         if (ic.live) tile_next(sch, ic);
         const Loc lc = locate(ic);

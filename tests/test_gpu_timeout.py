@@ -1,11 +1,12 @@
 """Failure detection on the device, without a GPU fault: a bounded wait that gives up.
 
-Every wait in the decode kernel is bounded; when one gives up the kernel raises
-GOLLEK_STATUS_TIMEOUT, stops, lets its issued copies land and returns, so the context stays
-usable.  These tests make one wait run out on purpose through two test hooks the library
-reads per call: GOLLEK_TEST_WAIT_LIMIT (a short bound for the waits) and
-GOLLEK_TEST_SKIP_GROUP (CTA 0's producer never issues that group's copies, so the consumer
-waiting for it gives up).  Nothing faults: the missing copy is simply never made.
+Every wait in the decode kernels and the tensor-memory multi-query kernel is bounded; when
+one gives up the kernel raises GOLLEK_STATUS_TIMEOUT, stops, lets its issued copies land and
+returns, so the context stays usable.  These tests make one wait run out on purpose through
+two test hooks the library reads per call: GOLLEK_TEST_WAIT_LIMIT (a short bound for the
+waits) and GOLLEK_TEST_SKIP_GROUP (CTA 0's producer never issues that group's -- for the
+tensor-memory kernel, that tile's -- copies, so the consumer waiting for it gives up).
+Nothing faults: the missing copy is simply never made.
 
 What is checked: the status word reports the timeout (and the synchronous legacy symbol
 returns GOLLEK_ERR_TIMEOUT), and the next normal call on the same split-K workspace --
@@ -90,3 +91,45 @@ def test_legacy_symbol_reports_the_timeout(cuda_device, monkeypatch):
     want = O.a1_execute(q, k, v, bt, ctx, 0.125)
     err = np.abs(out.cpu().numpy() - want).max()
     assert err <= 1e-4 * max(1.0, float(np.abs(want).max()))
+
+
+def test_tcgen05_multi_query_wait_gives_up_then_next_call_is_correct(cuda_device, monkeypatch):
+    """The tensor-memory multi-query kernel (64 folded rows: 16 queries x GQA 4): CTA 0's
+    producers never issue its first tile, so its score-MMA issuer's bounded wait gives up;
+    the kernel raises GOLLEK_STATUS_TIMEOUT, every warp of that CTA leaves, and the next
+    calls on the library's workspace (re-zeroed when the timeout is reported) match the
+    oracle."""
+    from gollek_b200 import _lib, ops
+    tq, hq, hkv = 16, 32, 8
+    q1, k, v, bt, ctx = decode_case([8000, 7000, 6000, 9000], hq=hq, hkv=hkv, d=128, bs=16, seed=63,
+                                    kv_std=0.5)
+    rng = np.random.default_rng(64)
+    q = O.round_bf16(rng.standard_normal((len(ctx), tq, hq, 128)).astype(np.float32))
+    kb, vb = O.round_bf16(k), O.round_bf16(v)
+    scale = 1.0 / math.sqrt(128)
+    want = O.a2_compute(q, kb, vb, bt, ctx, scale, num_kv_heads=hkv, block_size=16, causal=1,
+                        threads=O.num_threads())
+    dev = cuda_device
+    T = lambda x, dt=None: (torch.from_numpy(np.ascontiguousarray(x)).to(dev) if dt is None
+                            else torch.from_numpy(np.ascontiguousarray(x)).to(dev).to(dt))
+
+    def run():
+        return ops.paged_attention_prefill(T(q, torch.bfloat16), T(kb, torch.bfloat16), T(vb, torch.bfloat16),
+                                           T(bt), T(ctx), num_kv_heads=hkv, block_size=16, scale=scale,
+                                           causal=True, num_blocks=k.shape[0])
+
+    ops.device_status(dev.index, clear=True)
+    monkeypatch.setenv("GOLLEK_TEST_WAIT_LIMIT", "20000")
+    monkeypatch.setenv("GOLLEK_TEST_SKIP_GROUP", "0")
+    run()
+    torch.cuda.synchronize()
+    st = ops.device_status(dev.index, clear=True)
+    assert st & _lib.STATUS_TIMEOUT, st
+
+    monkeypatch.delenv("GOLLEK_TEST_WAIT_LIMIT")
+    monkeypatch.delenv("GOLLEK_TEST_SKIP_GROUP")
+    for _ in range(2):
+        out = run()
+        torch.cuda.synchronize()
+        assert ops.device_status(dev.index, clear=True) == 0
+        np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2, rtol=0)
