@@ -1114,9 +1114,10 @@ int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache
     p.workspace = ws;
     p.workspace_bytes = cap;
     // Page-once chunks: F queries of a sequence times its GQA group G as the rows of one
-    // (sequence, kv-head) unit of the decode kernel (G*F one of its row counts
-    // 2, 4, 8, and 16 for bf16 KV with head_dim 128), each row with its own causal limit,
-    // so a page is read once per F queries instead of once per query.  Causal, no sliding
+    // (sequence, kv-head) unit (G*F one of the decode kernel's row counts 2, 4, 8, and 16
+    // for bf16 KV with head_dim 128, or 32 or 64 on the tensor-memory kernel with bf16 q),
+    // each row with its own causal limit, so a page is read once per F queries instead of
+    // once per query.  Causal, no sliding
     // window (its start would differ per row), bf16/f16/fp32 KV or int8 KV with head_dim 128.
     // F is the largest power of two dividing Tq whose rows have a compiled kernel;
     // GOLLEK_PREFILL_FOLD=0 keeps one query per decode sequence.  The partial slots need
