@@ -77,6 +77,8 @@ def _build_locked(verbose: bool) -> str:
         cmd[1:1] = ["-ccbin", "/usr/bin/g++"]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     if r.returncode != 0:
+        if os.path.exists(tmp):
+            os.remove(tmp)
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("nvcc failed building libgollek_kernels.so")
     if verbose:
