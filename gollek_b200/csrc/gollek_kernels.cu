@@ -573,13 +573,23 @@ bool prefill_tc_enabled() {
     return !(e && e[0] == '0');
 }
 
+// GOLLEK_PREFILL_TC_HALVES=1 (read per call): the variant with two warps per 32 rows, one
+// per half of a tile's tokens (prefill_tc_kernel<G, true>); off by default.
+bool prefill_tc_halves() {
+    const char *e = std::getenv("GOLLEK_PREFILL_TC_HALVES");
+    return e && e[0] == '1';
+}
+
 int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
     if (!prefill_tc_enabled()) return kNotTaken;
     // (folded calls come without a window; decode may have one)
     if (p.kv_dtype != GOLLEK_DTYPE_BF16 || p.q_dtype != GOLLEK_DTYPE_BF16 || p.D != 128) return kNotTaken;
     if (G != 32 && G != 64) return kNotTaken;
-    const void *fn = G == 64 ? reinterpret_cast<const void *>(&prefill_tc_kernel<64>)
-                             : reinterpret_cast<const void *>(&prefill_tc_kernel<32>);
+    const bool halves = prefill_tc_halves();
+    const void *fn = G == 64 ? (halves ? reinterpret_cast<const void *>(&prefill_tc_kernel<64, true>)
+                                       : reinterpret_cast<const void *>(&prefill_tc_kernel<64>))
+                             : (halves ? reinterpret_cast<const void *>(&prefill_tc_kernel<32, true>)
+                                       : reinterpret_cast<const void *>(&prefill_tc_kernel<32>));
     if (!tma_layout_ok(p, page_stride) || !aligned16(p.q) || !aligned16(p.out)) return kNotTaken;
     const long long rows_per_page = page_stride / p.D;
     if (rows_per_page % 8 != 0) return kNotTaken;
@@ -588,7 +598,7 @@ int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
     int nk = 0, nv = 0;
     PtSmem L{};
     for (const auto &rg : kRings) {
-        L = pt_smem_layout(G, rg[0], rg[1], p.S, ctas);
+        L = pt_smem_layout(G, rg[0], rg[1], p.S, ctas, halves);
         if (L.total <= 227 * 1024) {
             nk = rg[0];
             nv = rg[1];

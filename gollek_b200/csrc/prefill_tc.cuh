@@ -33,6 +33,14 @@
 // wait for, and at a run's end each writes its own rows (a split run's last arriving warp
 // merges all rows).  Every wait is bounded and gives up once another warp has given up;
 // tensor memory is released only after both MMA issuers have drained.
+//
+// HALVES (opt-in, GOLLEK_PREFILL_TC_HALVES=1): two warps per 32 rows on the same SM
+// sub-partition, warp 4 + i taking tokens 0-63 of every tile and warp i tokens 64-127,
+// each with its own exponent reference, normaliser and O accumulator in tensor memory
+// (columns 256-383 and 384-511), so a tile's softmax pass is split over two warps whose
+// latencies overlap.  At a run's end warp i hands its (reference, normaliser) through
+// shared memory and warp 4 + i merges the two halves of its rows.  Warps 0 and 1 zero the
+// empty outputs before their rows.
 #pragma once
 
 #include <type_traits>
@@ -42,7 +50,7 @@
 namespace gk {
 
 constexpr int kPtThreads = 256;
-constexpr uint32_t kPtCols = 512;  // S x2 (128 columns each), O (128)
+constexpr uint32_t kPtCols = 512;  // S x2 (128 columns each), O (128; HALVES: two of them)
 
 // Waits suspend the waiting thread until the phase completes (up to this long per test),
 // which leaves the issue slots and the shared-memory pipe to the MMA issue, tensor-memory
@@ -55,12 +63,14 @@ constexpr uint32_t kPtSuspendNs = kSuspendNs;
 constexpr float kPtLazyMax = 8.f;
 
 struct PtSmem {
-    uint32_t q, p, kring, vring, prefix, cprefix, lens, rstart, misc, bars, total;
+    uint32_t q, p, kring, vring, prefix, cprefix, lens, rstart, misc, ml, bars, total;
 };
 
 // q [slab] and P [buffer][slab]: NQ rows of 128 bytes each, 1 KB aligned; the padding rows
-// of the last q slab read into P, those of the last P slab into the K ring.
-__host__ __device__ inline PtSmem pt_smem_layout(int nq, int kst, int vst, int num_seqs, int num_ctas) {
+// of the last q slab read into P, those of the last P slab into the K ring.  halves: the
+// second-half warps' (reference, normaliser) per row and their two hand-over barriers.
+__host__ __device__ inline PtSmem pt_smem_layout(int nq, int kst, int vst, int num_seqs, int num_ctas,
+                                                 bool halves = false) {
     PtSmem L;
     const uint32_t slab = static_cast<uint32_t>(nq) * 128;
     uint32_t o = 0;
@@ -83,25 +93,28 @@ __host__ __device__ inline PtSmem pt_smem_layout(int nq, int kst, int vst, int n
     o += (num_ctas + 1) * 8;
     L.misc = o;
     o += 64;
+    L.ml = o;
+    o += halves ? 2 * nq * 4 : 0;
     L.bars = o;
-    o += (2 * kst + 2 * vst + 12) * 8;
+    o += (2 * kst + 2 * vst + 12 + (halves ? 2 : 0)) * 8;
     L.total = o + 1024;  // slack to align the base to 1024 bytes
     return L;
 }
 
-template <int NQ>
+template <int NQ, bool HALVES = false>
 __global__ void __launch_bounds__(kPtThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const DecodeArgs a) {
     constexpr int D = 128;
-    constexpr int NW = NQ / 32;           // row warps
+    constexpr int NW = NQ / 32;           // row warps (per token half with HALVES)
+    constexpr int NRW = HALVES ? 2 * NW : NW;
     constexpr uint32_t kSlab = NQ * 128;  // one operand slab: NQ rows x 64 columns
     static_assert(NQ == 32 || NQ == 64, "rows per unit");
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int NK = a.num_stages;
     const int NV = a.num_vstages;
-    const PtSmem L = pt_smem_layout(NQ, NK, NV, a.num_seqs, gridDim.x);
+    const PtSmem L = pt_smem_layout(NQ, NK, NV, a.num_seqs, gridDim.x, HALVES);
     const uint32_t q_s = smem_u32(smem + L.q);
     const uint32_t p_s = smem_u32(smem + L.p);
     uint8_t *sm_kring = smem + L.kring;
@@ -124,6 +137,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     uint64_t *o_free = o_done + 2;    // [1] O read at a run's end
     uint64_t *q_full = o_free + 1;    // [1] q staged
     uint64_t *mma_done = q_full + 1;  // [2] score and value issuers drained
+    uint64_t *ml_full = mma_done + 2; // HALVES [NW]: second-half (reference, normaliser) written
+    float *sm_ml = reinterpret_cast<float *>(smem + L.ml);  // HALVES: [2][NQ]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -142,13 +157,15 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], NW);
-            mbar_init(&p_full[i], NW);
+            mbar_init(&s_free[i], NRW);
+            mbar_init(&p_full[i], NRW);
             mbar_init(&o_done[i], 1);
             mbar_init(&mma_done[i], 1);
         }
         mbar_init(o_free, NW);
         mbar_init(q_full, NW);
+        if constexpr (HALVES)
+            for (int i = 0; i < NW; ++i) mbar_init(&ml_full[i], 1);
         fence_barrier_init();
         sm_misc[1] = 0;
         sm_misc[3] = 0;
@@ -169,6 +186,15 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 
     // tries of a suspending wait (GOLLEK_TEST_WAIT_LIMIT shortens them, as for every wait)
     const unsigned it_tries = a.wait_limit ? max(1u, a.wait_limit >> 6) : kSuspendTries;
+
+    // Sequences with nothing to attend to: zeros, written by CTA s % grid (threads 0-63).
+    auto zero_empty = [&]() {
+        for (int s = blockIdx.x; s < S; s += gridDim.x) {
+            if (sm_prefix[s + 1] != sm_prefix[s]) continue;
+            for (int o = tid; o < Hkv * NQ * D; o += 64)
+                store_out(a.out, static_cast<long long>(s) * Hkv * NQ * D + o, 0.f, 1);
+        }
+    };
 
     if (warp == 2 || warp == 7) {
         // ========================================================= producers (K: warp 2, V: warp 7)
@@ -225,9 +251,13 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 const uint32_t vb = v_base + static_cast<uint32_t>(slot) * kTcTile;
                 const uint32_t pb = p_s + static_cast<uint32_t>(2 * sb) * kSlab;
 #pragma unroll
-                for (int kk = 0; kk < kTcTokens / 16; ++kk)
-                    umma_f16(t_o, umma_desc_sw128(pb + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024),
-                             umma_desc_sw128(vb + kk * 4096, 1024, 2048), id_o, (ip.tg0 > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < kTcTokens / 16; ++kk) {
+                    // HALVES: tokens 64-127 (kk >= 4) accumulate into the second O
+                    const uint32_t t_d = HALVES ? t_o + 128u * static_cast<uint32_t>(kk >> 2) : t_o;
+                    const bool acc = HALVES ? (ip.tg0 > 0 || (kk & 3) > 0) : (ip.tg0 > 0 || kk > 0);
+                    umma_f16(t_d, umma_desc_sw128(pb + (kk >> 2) * kSlab + (kk & 3) * 32, 16, 1024),
+                             umma_desc_sw128(vb + kk * 4096, 1024, 2048), id_o, acc ? 1u : 0u);
+                }
                 umma_commit(&o_done[sb]);
                 umma_commit(&v_empty[slot]);
             }
@@ -235,10 +265,16 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             mbar_wait(&mma_done[1], 0);
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 4 + NW) {
+    } else if ((warp >= 4 && warp < 4 + NW) || (HALVES && warp < NW)) {
         // ========================================================= row threads
-        const int c = 32 * (warp - 4) + lane;  // row = tensor-memory lane
-        const uint32_t t_lane = static_cast<uint32_t>(32 * (warp - 4)) << 16;
+        // sec: a HALVES second-half warp (tokens 64-127 of every tile; warps 0 .. NW-1)
+        const bool sec = HALVES && warp < 4;
+        const int half = sec ? 1 : 0;
+        if (sec) zero_empty();
+        // rows 32 (warp & 3) .. + 31: warp 4 + i and (HALVES) warp i share lane quarter i
+        const int c = 32 * (warp & 3) + lane;  // row = tensor-memory lane
+        const uint32_t t_lane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        const uint32_t t_om = HALVES ? t_o + 128u * static_cast<uint32_t>(half) : t_o;  // this warp's O
         const int gm = NQ / a.qfold;                 // heads per query
         const int qshift = a.qfold - 1 - c / gm;     // row c's query sees the positions before len - qshift
         const unsigned wl = a.wait_limit ? max(1u, a.wait_limit >> 6) : kSuspendTries;
@@ -263,7 +299,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             if (lane == 0) mbar_arrive(q_full);
             qx += rq.len;
         };
-        stage_next_q();
+        if (!sec) stage_next_q();
 
         // One pass over a tile's scores (tensor memory, 64 columns at a time): probabilities
         // exp2(d), d = x - mref (x: the score in the exp2 domain), of the tokens [lo, hi) as
@@ -277,7 +313,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             float dm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             float lsa[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int hh = 0; hh < (HALVES ? 1 : 2); ++hh) {
+                const int h = HALVES ? half : hh;  // HALVES: this warp's 64 tokens only
                 float v[64];
                 tmem_ld<32>(tmem + 128 * sb + 64 * h + t_lane, v);
                 tmem_ld<32>(tmem + 128 * sb + 64 * h + 32 + t_lane, v + 32);
@@ -313,7 +350,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         };
         auto run_pass = [&](int sb, int lo, int hi, float mref, float &dmax, float &ls) {
             // warp-uniform choice (the pass holds warp-collective tensor-memory loads)
-            const bool mask = __any_sync(0xffffffffu, lo > 0 || hi < kTcTokens);
+            const bool mask = __any_sync(0xffffffffu, HALVES ? (lo > 64 * half || hi < 64 * half + 64)
+                                                             : (lo > 0 || hi < kTcTokens));
             using T = std::true_type;
             using F = std::false_type;
             if (cap) {
@@ -333,7 +371,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         auto tile_max = [&](int sb, int lo, int hi) {
             float m = -INFINITY;
 #pragma unroll 1
-            for (int k = 0; k < 4; ++k) {
+            for (int k = HALVES ? 2 * half : 0; k < (HALVES ? 2 * half + 2 : 4); ++k) {
                 float v[32];
                 tmem_ld<32>(tmem + 128 * sb + 32 * k + t_lane, v);
                 tmem_wait_ld();
@@ -349,6 +387,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         bool bad = false;         // a wait of this warp gave up
         for (TileIt it = tile_begin(sch); it.live;) {
             const int ti = it.ti;
+            [[maybe_unused]] const int ri = it.ri;  // run index within this CTA (HALVES hand-over)
             const int sb = ti & 1;
             const Run r = it.r;
             const int ng = min(kTcGroups, r.len - it.tg0);
@@ -391,18 +430,18 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll 1
                     for (int k = 0; k < 4; ++k) {
                         float o[32];
-                        tmem_ld<32>(t_o + 32 * k + t_lane, o);
+                        tmem_ld<32>(t_om + 32 * k + t_lane, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] *= alpha;
-                        tmem_st32(t_o + 32 * k + t_lane, o);
+                        tmem_st32(t_om + 32 * k + t_lane, o);
                     }
                     tmem_wait_st();
                 }
                 run_pass(sb, lo, hi, m_run == -INFINITY ? 0.f : m_run, dmax, ls);
             }
             l_run += ls;
-            if (lo > 0 || vhi < kTcTokens) {
+            if (!sec && (lo > 0 || vhi < kTcTokens)) {
                 // clear V rows [0, lo) and [vhi, 128) once the tile's V copies have landed
                 const int vslot = ti % NV;
                 if (!warp_wait(&v_full[vslot], (ti / NV) & 1, wl, abort, kPtSuspendNs)) {
@@ -425,21 +464,57 @@ __global__ void __launch_bounds__(kPtThreads, 1)
             tile_next(sch, it);
             if (!run_end) continue;
 
+            if constexpr (HALVES) {
+                if (sec) {
+                    // second half: hand (reference, normaliser) of row c to warp 4 + (warp & 3)
+                    // (read before it stages the next run's q, so before this warp's
+                    // next run can end and write them again)
+                    sm_ml[c] = m_run;
+                    sm_ml[NQ + c] = l_run;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ml_full[warp & 3]);
+                    m_run = -INFINITY;
+                    l_run = 0.f;
+                    continue;
+                }
+            }
             // ---------------- end of the run: row c of O, normalised, out
             if (!warp_wait(&o_done[sb], (ti >> 1) & 1, wl, abort, kPtSuspendNs)) {
                 bad = true;
                 break;
             }
+            // HALVES: the two halves of row c against their common maximum mm
+            float mm = m_run, lsum = l_run;
+            [[maybe_unused]] float fa = 1.f, fb = 0.f;
+            if constexpr (HALVES) {
+                if (!warp_wait(&ml_full[warp & 3], ri & 1, wl, abort, kPtSuspendNs)) {
+                    bad = true;
+                    break;
+                }
+                const float mb = sm_ml[c], lb = sm_ml[NQ + c];
+                mm = fmaxf(m_run, mb);
+                fa = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mm);
+                fb = mb == -INFINITY ? 0.f : fast_exp2(mb - mm);
+                lsum = l_run * fa + lb * fb;
+            }
             tc_fence_after();
             const long long unit = static_cast<long long>(r.s) * Hkv + r.h;
             float *part = a.partials + (unit * kMaxSplits + r.piece) * slot_floats;
             const long long out_row = qo_row(r.s, r.h, c, Hkv, NQ, a.qfold, a.seq_div) * D;
-            const float inv = l_run > 0.f ? 1.0f / (l_run + a.norm_eps) : 0.f;
+            const float inv = lsum > 0.f ? 1.0f / (lsum + a.norm_eps) : 0.f;
 #pragma unroll 1
             for (int k = 0; k < 4; ++k) {
                 float o[32];
                 tmem_ld<32>(t_o + 32 * k + t_lane, o);
-                tmem_wait_ld();
+                if constexpr (HALVES) {
+                    float ob[32];
+                    tmem_ld<32>(t_o + 128 + 32 * k + t_lane, ob);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = fmaf(o[i], fa, ob[i] * fb);
+                } else {
+                    tmem_wait_ld();
+                }
                 if (r.pieces == 1) {
                     uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(a.out) + out_row + 32 * k);
 #pragma unroll
@@ -462,8 +537,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
                 // Each row warp of each piece arrives on the unit's counter once its rows of
                 // the partial are written; the last of the pieces x NW arrivals merges all
                 // rows (log-sum-exp), so no warp waits for another.
-                part[c] = m_run;
-                part[NQ + c] = l_run;
+                part[c] = mm;
+                part[NQ + c] = lsum;
                 __threadfence();
                 __syncwarp();
                 int old = 0;
@@ -518,13 +593,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         }
         if (bad && lane == 0) *abort = 1;
     } else if (warp < 2) {
-        // ========================================================= warps 0, 1
-        // Sequences with nothing to attend to: zeros, written by CTA s % grid.
-        for (int s = blockIdx.x; s < S; s += gridDim.x) {
-            if (sm_prefix[s + 1] != sm_prefix[s]) continue;
-            for (int o = tid; o < Hkv * NQ * D; o += 64)
-                store_out(a.out, static_cast<long long>(s) * Hkv * NQ * D + o, 0.f, 1);
-        }
+        // ========================================================= warps 0, 1 (not rows)
+        zero_empty();
     }
 
     // ------------------------------------------------------------ teardown
