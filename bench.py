@@ -1024,7 +1024,9 @@ def bench_prefill(args, world, rank, local):
                 fold = f
                 break
             f >>= 1
-    kernel = ("prefill_tc_kernel (tcgen05; the folded rows are the MMA rows)" if fold * G in (32, 64)
+    halves = os.environ.get("GOLLEK_PREFILL_TC_HALVES", "1") != "0"
+    kernel = (f"prefill_tc_kernel (tcgen05; the folded rows are the MMA rows; {2 if halves else 1} "
+              "warp(s) per 32 rows)" if fold * G in (32, 64)
               else "decode_tma_kernel (queries folded into the MMA rows)" if fold > 1
               else "decode_tma_kernel (per-query decode sequences)")
     kv_once = batch.algorithmic_bytes() - 2 * batch.q.numel() * batch.q_elem

@@ -573,11 +573,12 @@ bool prefill_tc_enabled() {
     return !(e && e[0] == '0');
 }
 
-// GOLLEK_PREFILL_TC_HALVES=1 (read per call): the variant with two warps per 32 rows, one
-// per half of a tile's tokens (prefill_tc_kernel<G, true>); off by default.
+// Two warps per 32 rows, one per half of a tile's tokens (prefill_tc_kernel<G, true>):
+// 0.339 against 0.503 ms at Tq = 16 on config 2's pool.  GOLLEK_PREFILL_TC_HALVES=0 (read
+// per call) selects one warp per 32 rows.
 bool prefill_tc_halves() {
     const char *e = std::getenv("GOLLEK_PREFILL_TC_HALVES");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
 }
 
 int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
@@ -585,27 +586,35 @@ int try_prefill_tc(const V2 &p, int dev, int G, long long page_stride) {
     // (folded calls come without a window; decode may have one)
     if (p.kv_dtype != GOLLEK_DTYPE_BF16 || p.q_dtype != GOLLEK_DTYPE_BF16 || p.D != 128) return kNotTaken;
     if (G != 32 && G != 64) return kNotTaken;
-    const bool halves = prefill_tc_halves();
-    const void *fn = G == 64 ? (halves ? reinterpret_cast<const void *>(&prefill_tc_kernel<64, true>)
-                                       : reinterpret_cast<const void *>(&prefill_tc_kernel<64>))
-                             : (halves ? reinterpret_cast<const void *>(&prefill_tc_kernel<32, true>)
-                                       : reinterpret_cast<const void *>(&prefill_tc_kernel<32>));
     if (!tma_layout_ok(p, page_stride) || !aligned16(p.q) || !aligned16(p.out)) return kNotTaken;
     const long long rows_per_page = page_stride / p.D;
     if (rows_per_page % 8 != 0) return kNotTaken;
     const int ctas = sm_count(dev);
+    // the largest rings that fit, two warps per 32 rows first; their hand-over area costs
+    // 2 * G floats, so a call with slightly more sequences runs the one-warp form
     static const int kRings[][2] = {{2, 3}, {2, 2}, {1, 2}};
     int nk = 0, nv = 0;
     PtSmem L{};
-    for (const auto &rg : kRings) {
-        L = pt_smem_layout(G, rg[0], rg[1], p.S, ctas, halves);
-        if (L.total <= 227 * 1024) {
-            nk = rg[0];
-            nv = rg[1];
-            break;
+    bool halves = prefill_tc_halves();
+    for (int form = 0; form < 2 && !nk; ++form) {
+        if (form == 1) {
+            if (!halves) break;
+            halves = false;
+        }
+        for (const auto &rg : kRings) {
+            L = pt_smem_layout(G, rg[0], rg[1], p.S, ctas, halves);
+            if (L.total <= 227 * 1024) {
+                nk = rg[0];
+                nv = rg[1];
+                break;
+            }
         }
     }
     if (!nk) return kNotTaken;
+    const void *fn = G == 64 ? (halves ? reinterpret_cast<const void *>(&prefill_tc_kernel<64, true>)
+                                       : reinterpret_cast<const void *>(&prefill_tc_kernel<64>))
+                             : (halves ? reinterpret_cast<const void *>(&prefill_tc_kernel<32, true>)
+                                       : reinterpret_cast<const void *>(&prefill_tc_kernel<32>));
     void *ws = nullptr;
     size_t ws_cap = 0;
     int rc = v2_workspace(p, dev, &ws, &ws_cap);

@@ -28,13 +28,14 @@
 //   warp 6 lane 0 issues the value MMAs (overwriting O at a run's first tile);
 //   warps 4 .. 4 + NQ/32 - 1 (tensor-memory lane quarters 0, 1): row threads, whose
 //     sub-partitions hold no producer or issuer;
-//   warps 0, 1 (and 5 when NQ = 32): zero the outputs of empty sequences, then idle.
+//   warps 0, 1: zero the outputs of empty sequences; then (HALVES) warps 0 .. NQ/32 - 1
+//     take the second half of the rows' tokens, and the remaining warps idle.
 // The row warps never wait for one another: each arrives on the barriers the MMA issuers
 // wait for, and at a run's end each writes its own rows (a split run's last arriving warp
 // merges all rows).  Every wait is bounded and gives up once another warp has given up;
 // tensor memory is released only after both MMA issuers have drained.
 //
-// HALVES (opt-in, GOLLEK_PREFILL_TC_HALVES=1): two warps per 32 rows on the same SM
+// HALVES (the default; GOLLEK_PREFILL_TC_HALVES=0: off): two warps per 32 rows on the same SM
 // sub-partition, warp 4 + i taking tokens 0-63 of every tile and warp i tokens 64-127,
 // each with its own exponent reference, normaliser and O accumulator in tensor memory
 // (columns 256-383 and 384-511), so a tile's softmax pass is split over two warps whose

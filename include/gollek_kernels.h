@@ -168,7 +168,8 @@ GOLLEK_API size_t gollek_paged_attention_workspace_size(int num_seqs, int num_q_
  * head_dim 128, on the tcgen05 kernel) queries of a sequence share one pass over its pages
  * as extra rows, each row with its own causal bound.  Other calls read each query's
  * context once per query.  The environment variables GOLLEK_PREFILL_FOLD=0 (read per call)
- * select the per-query form everywhere, GOLLEK_PREFILL_TC=0 the <= 16-row passes only.
+ * select the per-query form everywhere, GOLLEK_PREFILL_TC=0 the <= 16-row passes only,
+ * GOLLEK_PREFILL_TC_HALVES=0 one warp per 32 rows on the tcgen05 kernel (two by default).
  */
 GOLLEK_API int gollek_paged_attention_prefill(void *out, const void *q, const void *k_cache,
                                    const void *v_cache, const float *k_scales, const float *v_scales,

@@ -121,7 +121,9 @@ def test_bf16_large_groups(cuda_device, monkeypatch, hq, hkv, window, soft_cap, 
     """Decode with 32 or 64 q heads per kv head (multi-query-attention models): the
     tensor-memory kernel of prefill_tc.cuh with the heads as its rows, against the oracle,
     twice (bit-identical); windows and soft-cap; pages of 8, 16 and 64 tokens; an empty
-    context gives zeros; the 9000-token context splits across CTAs.  No other kernel serves these groups: with
+    context gives zeros; the 9000-token context splits across CTAs.  Both forms of the kernel:
+    two warps per 32 heads, one per half of a tile's tokens (the default), and one warp
+    (GOLLEK_PREFILL_TC_HALVES=0).  No other kernel serves these groups: with
     GOLLEK_PREFILL_TC=0 the call is refused as unsupported."""
     from gollek_b200 import ops
     ctx = [1, 31, 32, 33, 200, 517, 1024, 2049, 0, 77, 9000]
@@ -138,9 +140,13 @@ def test_bf16_large_groups(cuda_device, monkeypatch, hq, hkv, window, soft_cap, 
         return out.float().cpu().numpy()
 
     tc = [run(), run()]
-    for got in tc:
+    monkeypatch.setenv("GOLLEK_PREFILL_TC_HALVES", "0")
+    one = run()
+    monkeypatch.delenv("GOLLEK_PREFILL_TC_HALVES")
+    for got in tc + [one]:
         np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
     np.testing.assert_array_equal(tc[0], tc[1])
+    assert not one[8].any()
     monkeypatch.setenv("GOLLEK_PREFILL_TC", "0")
     from gollek_b200 import _lib
     with pytest.raises(_lib.GollekError) as err:

@@ -256,8 +256,10 @@ def _nan_past_context(k, v, bt, ctx, bs=16):
                                                    (32, 8, 16, 0.0, 8), (32, 8, 8, 0.0, 32)])
 def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap, bs):
     """Folded calls of 32 or 64 rows (F queries x G heads) per (chunk, kv-head): the
-    tensor-memory kernel (prefill_tc.cuh), against the oracle and against the same call on
-    the 16-row mma.sync fold (GOLLEK_PREFILL_TC=0).  Lengths below Tq give rows that see
+    tensor-memory kernel (prefill_tc.cuh) in both forms -- two warps per 32 rows, one per
+    half of a tile's tokens (the default), and one warp (GOLLEK_PREFILL_TC_HALVES=0) --
+    against the oracle and against the same call on the 16-row mma.sync fold
+    (GOLLEK_PREFILL_TC=0).  Lengths below Tq give rows that see
     nothing or part of a tile; NaN fills the page rows past every context; the 6000-token
     sequence splits across CTAs (merged by the last piece); Tq = 48 gives three 16-query
     chunks per sequence."""
@@ -277,11 +279,15 @@ def test_prefill_tc_rows(cuda_device, monkeypatch, hq, hkv, tq, soft_cap, bs):
                                            soft_cap=soft_cap).float().cpu().numpy()
 
     tc = [run() for _ in range(2)]
+    monkeypatch.setenv("GOLLEK_PREFILL_TC_HALVES", "0")
+    one = run()
+    monkeypatch.delenv("GOLLEK_PREFILL_TC_HALVES")
     monkeypatch.setenv("GOLLEK_PREFILL_TC", "0")
     mma = run()
-    for got in tc + [mma]:
+    for got in tc + [one, mma]:
         assert np.isfinite(got).all()
         np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
     np.testing.assert_allclose(tc[0], mma, atol=1e-2, rtol=0)
+    np.testing.assert_allclose(tc[0], one, atol=1e-2, rtol=0)
     assert not tc[0][0, :max(0, tq - 2)].any()
     assert ops.device_status(cuda_device.index or 0) == 0
